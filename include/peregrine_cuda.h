@@ -1,0 +1,252 @@
+/*
+ * peregrine_cuda.h — C ABI of libperegrine_cuda.so, the B200 (sm_100a) KV / prefix-cache
+ * hot path of the Peregrine Qwen3.5-9B server.
+ *
+ * The reference binds its GPU work through the Objective-C Metal bridge
+ * (src/runtime/bridge.h:1-103) and through Zig helpers that copy cache state with host
+ * memcpy (src/model/state.zig:124-230). Each entry point below names the reference
+ * interface it replaces.
+ *
+ * Conventions (mirroring src/runtime/bridge.h):
+ *   - plain pointers and sizes only; bf16 tensors are passed as uint16_t bit patterns;
+ *   - the caller owns every device, pinned-host and workspace buffer;
+ *   - every operation is enqueued asynchronously on the caller's CUDA stream
+ *     (a cudaStream_t passed as void*; NULL = legacy default stream);
+ *   - every entry returns an int status: 0 = ok, negative = PGC_ERR_* (the reference's
+ *     encode calls return void and report GPU failure at commit time, bridge.m:376;
+ *     here shape and bounds errors are caught on the host before the launch);
+ *   - device-side faults never trap: kernels that find an out-of-range index record it
+ *     in a device error word (read with pgc_device_error) and skip the access.
+ *
+ * Fixed geometry (Qwen3.5-9B full-attention layers, src/model/block_attn.zig:21-28):
+ * 16 query heads, 4 KV heads (GQA group 4), head_dim 256, rotary_dim 64, hidden 4096.
+ *
+ * Paged KV layout (new design; the reference cache is a dense strided buffer, see
+ * state.zig:41-44): per layer one K pool and one V pool, each
+ *     pool[page][kv_head 4][slot 16][dim 256]  bf16
+ * so one (page, kv head) is an 8 KiB contiguous run of 16 token rows of 512 B. A token at
+ * logical position t of a sequence lives in page block_table[t / 16], slot t % 16.
+ */
+#ifndef PEREGRINE_CUDA_H
+#define PEREGRINE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PGC_NUM_Q_HEADS 16
+#define PGC_NUM_KV_HEADS 4
+#define PGC_GQA_GROUP 4
+#define PGC_HEAD_DIM 256
+#define PGC_ROTARY_DIM 64
+#define PGC_PAGE_TOKENS 16
+#define PGC_HIDDEN 4096
+#define PGC_MAX_CONTEXT_TOKENS 65536 /* state.zig:11 (per-sequence dense cache limit) */
+#define PGC_PARTIAL_FLOATS (PGC_HEAD_DIM + 2) /* one (m, l, o[256]) partial */
+#define PGC_MAX_QUERIES 4                     /* query tokens per sequence per decode call */
+#define PGC_MAX_REGIONS 128                   /* regions per pgc_copy_regions call */
+
+enum pgc_status {
+    PGC_OK = 0,
+    PGC_ERR_INVALID = -1,   /* null pointer, bad shape or unsupported parameter */
+    PGC_ERR_BOUNDS = -2,    /* index or length outside the buffer it addresses */
+    PGC_ERR_WORKSPACE = -3, /* workspace smaller than the *_workspace_bytes query */
+    PGC_ERR_CUDA = -4,      /* a CUDA runtime/driver call failed */
+    PGC_ERR_ALIGN = -5,     /* a pointer or size lacks the required alignment */
+    PGC_ERR_DEVICE = -6,    /* current device is not sm_100 */
+    PGC_ERR_TIMEOUT = -7,   /* a bounded device wait gave up (reported by pgc_device_error) */
+    PGC_ERR_CONTEXT = -8    /* length outside (0, PGC_MAX_CONTEXT_TOKENS] */
+};
+
+/* Status text for an error code (static storage). */
+const char *pgc_status_string(int status);
+/* Library ABI version (major*10000 + minor*100 + patch). */
+int pgc_version(void);
+/* Reads and optionally clears the device error word of the current device: 0 when no kernel
+ * recorded a fault. Synchronises the device. Replaces the reference's
+ * MTLCommandBufferStatusError check at commit time (bridge.m:376). */
+int pgc_device_error(int *code_out, int64_t *detail_out, int clear);
+
+/* ---------------------------------------------------------------------------------------
+ * Layout rules
+ * ------------------------------------------------------------------------------------- */
+
+/* Dense-cache token stride for a sequence capacity; replaces fullCacheStrideForMaxSeq
+ * (src/model/state.zig:25-32): align(max_seq, 256), or align(max_seq, 64) once
+ * max_seq >= 16000; PGC_ERR_CONTEXT for 0 or > 65536. Used by the dense snapshot format. */
+int pgc_full_cache_stride_for_max_seq(uint64_t max_seq, uint64_t *stride_out);
+
+/* Fills a RoPE cos/sin table [max_pos][rot_dim] fp32 on the HOST: row p holds
+ * cos(p * theta^(-2i/rot_dim)) for i < rot_dim/2 followed by the matching sines, each
+ * computed in double and rounded once to fp32. Replaces the per-thread pow/cos/sin of
+ * shaders/rope.metal:5-10 and attention.metal:391-396 with a table built once per model;
+ * the append kernel reads it, so device and host agree bit for bit. */
+int pgc_rope_table_fill(float *table_host, int64_t max_pos, int rot_dim, double theta);
+
+/* ---------------------------------------------------------------------------------------
+ * A3/A4: KV append with fused RMSNorm + partial RoPE
+ * ------------------------------------------------------------------------------------- */
+
+#define PGC_APPEND_DECODE 0  /* qwen35_q_gate_prepare_kv_append_pair_..._bf16 rounding */
+#define PGC_APPEND_PREFILL 1 /* qwen35_qk_norm_rope_append_many_bf16 rounding */
+
+/* Prepares `tokens` new rows: for each token t, each of the 16 q heads and the 4 k heads is
+ * optionally RMS-normalised (x * rsqrt(mean(x^2) + 1e-6) * w, tree-ordered sum of
+ * squares), then its first 64 dims get NeoX half-split RoPE at positions[t]; q goes to
+ * q_out, k to the K pool at slot_mapping[t] (= page * 16 + slot), v is copied unchanged
+ * to the V pool at the same slot. A negative slot skips the K/V write of that token.
+ *   q_in       [tokens][16][q_head_stride] bf16; q_head_stride 256, or 512 for the packed
+ *              q|gate projection of the decode path (attention.metal:362-366)
+ *   gate_out   nullable [tokens][16][256]: receives the gate half of a packed q_in
+ *   k_in, v_in [tokens][4][256]
+ *   q_norm_w, k_norm_w  nullable [256] bf16 RMSNorm weights (NULL = no norm)
+ *   rope_table [rope_max_pos][64] from pgc_rope_table_fill, in device memory
+ *   mode       PGC_APPEND_DECODE rounds the normalised pair to bf16 before rotating
+ *              (attention.metal:389-390); PGC_APPEND_PREFILL does not (attention.metal:196-197)
+ * Replaces: qwen35_q_gate_prepare_kv_append_pair_head_major_value_dim_major_bf16
+ * (shaders/attention.metal:327-421, launched at src/model/block_attn.zig:322-327) and
+ * qwen35_qk_norm_rope_append_many_bf16 (shaders/attention.metal:146-219, launched at
+ * src/model/block_attn.zig:435-441). */
+int pgc_append_kv_rope(const uint16_t *q_in, int q_head_stride, uint16_t *q_out,
+                       uint16_t *gate_out, const uint16_t *k_in, const uint16_t *v_in,
+                       const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                       const float *rope_table, int64_t rope_max_pos,
+                       const int32_t *positions, const int64_t *slot_mapping, int64_t tokens,
+                       uint16_t *k_pages, uint16_t *v_pages, int64_t num_pages, int mode,
+                       void *stream);
+
+/* ---------------------------------------------------------------------------------------
+ * A1/A2: split-K flash-decode attention over the paged cache
+ * ------------------------------------------------------------------------------------- */
+
+/* Workspace bytes pgc_decode_attn / pgc_decode_attn_partials need for this shape. */
+size_t pgc_decode_workspace_bytes(int batch, int num_queries, int max_seq_len);
+
+/* Decode SDPA for `batch` sequences, each with `num_queries` (1..4) consecutive query
+ * tokens (1 for a decode step, 2 for the MTP verify of draft + bonus). Query j of sequence
+ * b sits at position seq_lens[b] - num_queries + j and attends causally to tokens
+ * [0, seq_lens[b] - num_queries + j]. Scores are scale * q.k (fp32), softmax and the
+ * weighted V sum accumulate in fp32 and the output is rounded once to bf16; with a gate,
+ * out = attn * sigmoid(gate) (attention_decode.metal:240-242).
+ *   q            [batch][num_queries][16][256] bf16 (device)
+ *   k/v_pages    paged pools of `num_pages` pages (layout in the file header)
+ *   block_tables [batch][max_pages_per_seq] int32 page ids (device)
+ *   seq_lens     [batch] int32 tokens in cache including the queries (device)
+ *   max_seq_len  host-side upper bound of seq_lens (sizes the split grid)
+ *   gate         nullable [batch][num_queries][16][256] bf16
+ *   out          [batch][num_queries][16][256] bf16
+ * Replaces: sdpa_decode_prefix_flash_partials_bf16 (shaders/attention_decode.metal:24-210)
+ * + sdpa_decode_prefix_flash_reduce_gated_bf16 (:215-243), dispatched at
+ * src/model/block_attn.zig:331-356. The reference's two KV sources (prefix entry for
+ * t < prefix_len, request-local cache after, attention_decode.metal:89-93) become block
+ * table entries: shared prefix pages followed by request-local pages. */
+int pgc_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                    int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
+                    const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
+                    float scale, const uint16_t *gate, uint16_t *out, void *workspace,
+                    size_t workspace_bytes, void *stream);
+
+/* Same attention, but emits the un-normalised per-row partial (m, l, o[256]) fp32 of this
+ * cache instead of bf16 output: partials [batch][num_queries*16][258], m in natural-log
+ * units, l = sum exp(s - m), o = sum exp(s - m) v. Used for context-parallel shards, whose
+ * partials are exchanged and combined with pgc_merge_partials. Same partial format as
+ * attention_decode.metal:198-206. */
+int pgc_decode_attn_partials(const uint16_t *q, const uint16_t *k_pages,
+                             const uint16_t *v_pages, int64_t num_pages,
+                             const int32_t *block_tables, int max_pages_per_seq,
+                             const int32_t *seq_lens, int batch, int num_queries,
+                             int max_seq_len, float scale, float *partials, void *workspace,
+                             size_t workspace_bytes, void *stream);
+
+/* Log-sum-exp merge of `num_parts` partials per row: m* = max m_p, w_p = exp(m_p - m*),
+ * out = sum w_p o_p / sum w_p l_p, times sigmoid(gate) when gate is non-NULL, rounded to
+ * bf16. A part with m = -inf has weight 0. Row r, part p lives at
+ * partials + p * part_stride + r * 258 (floats). Replaces
+ * sdpa_decode_prefix_flash_reduce_gated_bf16 (shaders/attention_decode.metal:215-243) for
+ * partials that came from several GPUs. */
+int pgc_merge_partials(const float *partials, int64_t rows, int num_parts,
+                       int64_t part_stride, const uint16_t *gate, uint16_t *out,
+                       void *stream);
+
+/* ---------------------------------------------------------------------------------------
+ * A6-A9, A11: cache copies (prefix snapshot / restore, hidden rows, state)
+ * ------------------------------------------------------------------------------------- */
+
+/* Row gather/scatter: for i < n_rows, copies row_bytes from src + src_rows[i]*src_pitch to
+ * dst + dst_rows[i]*dst_pitch (a NULL index array means the identity). Any pointer the GPU
+ * can address: HBM, or pinned host memory (the host-resident prefix store). 16-byte vector
+ * path when pointers, pitches and row_bytes are 16-byte aligned, else a 4- or 1-byte path.
+ * Replaces the hidden-row memcpys of src/server/prefix_state_cache.zig:592-629, :477-487,
+ * :265-289 and src/server.zig:1263-1270, and serves page-granular KV copies
+ * (row = one (page) of a pool: 4 * 16 * 256 * 2 = 32 KiB). */
+int pgc_copy_rows(void *dst, const void *src, const int32_t *dst_rows,
+                  const int32_t *src_rows, int64_t n_rows, int64_t row_bytes,
+                  int64_t dst_pitch, int64_t src_pitch, void *stream);
+
+/* Restores `count` tokens from a dense reference-layout cache (K [4][src_stride][256]
+ * head-major, V [4][256][src_stride] value-dim-major, state.zig:41-44 and the v3 snapshot
+ * runs of src/server/prefix_persist.zig:85-137) starting at src_token into the paged pools
+ * at logical positions [dst_token, dst_token + count) of the sequence whose page ids are
+ * block_table[0 .. n_table). Replaces copyFullAttentionRangeFrom
+ * (src/model/state.zig:143-230) when the destination is the paged cache. */
+int pgc_kv_restore_dense(const uint16_t *k_dense, const uint16_t *v_dense,
+                         int64_t src_stride, int64_t src_token, uint16_t *k_pages,
+                         uint16_t *v_pages, int64_t num_pages, const int32_t *block_table,
+                         int64_t n_table, int64_t dst_token, int64_t count, void *stream);
+
+/* The inverse of pgc_kv_restore_dense: paged tokens [src_token, src_token + count) →
+ * dense reference layout at dst_token (storePrefixFromWork into a prefix entry,
+ * src/server/prefix_state_cache.zig:584-588, and the v3 persist writer). */
+int pgc_kv_snapshot_dense(const uint16_t *k_pages, const uint16_t *v_pages,
+                          int64_t num_pages, const int32_t *block_table, int64_t n_table,
+                          int64_t src_token, uint16_t *k_dense, uint16_t *v_dense,
+                          int64_t dst_stride, int64_t dst_token, int64_t count, void *stream);
+
+/* Copies logical tokens [src_token, src_token + count) of one paged sequence into logical
+ * tokens [dst_token, dst_token + count) of another (possibly the same pools). Replaces
+ * copyFullAttentionRangeFrom (src/model/state.zig:143-179) between two paged states, e.g.
+ * the verifier re-sync of src/server/decode_loop.zig:295-311. */
+int pgc_kv_copy_tokens(const uint16_t *src_k_pages, const uint16_t *src_v_pages,
+                       int64_t src_num_pages, const int32_t *src_table, int64_t src_n_table,
+                       int64_t src_token, uint16_t *dst_k_pages, uint16_t *dst_v_pages,
+                       int64_t dst_num_pages, const int32_t *dst_table, int64_t dst_n_table,
+                       int64_t dst_token, int64_t count, void *stream);
+
+/* One contiguous byte region. */
+typedef struct pgc_region {
+    void *dst;
+    const void *src; /* ignored by pgc_zero_regions */
+    uint64_t bytes;
+} pgc_region;
+
+/* Copies up to PGC_MAX_REGIONS regions in ONE launch (the descriptors travel as a kernel
+ * argument; no device descriptor buffer). Replaces copyLinearStateFrom
+ * (src/model/state.zig:130-141): 24 linear layers × (conv, recurrent) state. */
+int pgc_copy_regions(const pgc_region *regions_host, int n, void *stream);
+
+/* Zero-fills up to PGC_MAX_REGIONS regions in one launch. Replaces resetForNewSequence
+ * (src/model/state.zig:110-118) and the zero-fill of initBf16FullCaches (:51-83). */
+int pgc_zero_regions(const pgc_region *regions_host, int n, void *stream);
+
+/* ---------------------------------------------------------------------------------------
+ * A10: MTP verify rollback
+ * ------------------------------------------------------------------------------------- */
+
+/* Device-side accept/reject of a speculative verify step, with no host round trip.
+ * Reads *accept (device int32). When it is 0 (draft rejected): seq_lens[seq_index] -= reject_tokens
+ * (the rejected KV rows are truncated; attention is bounded by seq_len, so the rows need no
+ * clearing, state.zig:107-109) and every region is copied snapshot → live (regions[i].src =
+ * snapshot taken before the step, .dst = live recurrent/conv state). When *accept != 0
+ * nothing changes. Replaces the double-buffered swap + prepareVerifierState re-sync of
+ * src/server/decode_loop.zig:216-258,295-311. */
+int pgc_rollback(const int32_t *accept, int32_t *seq_lens, int seq_index, int reject_tokens,
+                 const pgc_region *regions_host, int n, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PEREGRINE_CUDA_H */

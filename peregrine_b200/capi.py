@@ -1,0 +1,247 @@
+"""ctypes binding of libperegrine_cuda.so (the C ABI in include/peregrine_cuda.h).
+
+This module only loads the native library and forwards raw pointers; it holds no compute of
+its own. Loading fails loudly when the library has not been built: there is no Python or CPU
+fallback for any operation.
+
+The thin tensor helpers at the bottom accept torch CUDA tensors (torch is used only as the
+device-memory allocator and stream source) and raise PgcError on a non-zero status.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libperegrine_cuda.so"
+
+HEAD_DIM = 256
+NUM_Q_HEADS = 16
+NUM_KV_HEADS = 4
+GQA_GROUP = 4
+ROTARY_DIM = 64
+PAGE_TOKENS = 16
+HIDDEN = 4096
+MAX_CONTEXT_TOKENS = 65536
+PARTIAL_FLOATS = HEAD_DIM + 2
+MAX_QUERIES = 4
+MAX_REGIONS = 128
+APPEND_DECODE = 0
+APPEND_PREFILL = 1
+
+STATUS = {
+    0: "PGC_OK", -1: "PGC_ERR_INVALID", -2: "PGC_ERR_BOUNDS", -3: "PGC_ERR_WORKSPACE",
+    -4: "PGC_ERR_CUDA", -5: "PGC_ERR_ALIGN", -6: "PGC_ERR_DEVICE", -7: "PGC_ERR_TIMEOUT",
+    -8: "PGC_ERR_CONTEXT",
+}
+
+
+class PgcError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {STATUS.get(status, status)}")
+
+
+class Region(C.Structure):
+    _fields_ = [("dst", C.c_void_p), ("src", C.c_void_p), ("bytes", C.c_uint64)]
+
+
+P = C.c_void_p
+I32 = C.c_int
+I64 = C.c_int64
+U64 = C.c_uint64
+F32 = C.c_float
+F64 = C.c_double
+SZ = C.c_size_t
+
+SIGNATURES = {
+    "pgc_status_string": (C.c_char_p, [I32]),
+    "pgc_version": (I32, []),
+    "pgc_device_error": (I32, [C.POINTER(I32), C.POINTER(I64), I32]),
+    "pgc_full_cache_stride_for_max_seq": (I32, [U64, C.POINTER(U64)]),
+    "pgc_rope_table_fill": (I32, [P, I64, I32, F64]),
+    "pgc_append_kv_rope": (I32, [P, I32, P, P, P, P, P, P, P, I64, P, P, I64, P, P, I64, I32, P]),
+    "pgc_decode_workspace_bytes": (SZ, [I32, I32, I32]),
+    "pgc_decode_attn": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, P, SZ, P]),
+    "pgc_decode_attn_partials": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, SZ, P]),
+    "pgc_merge_partials": (I32, [P, I64, I32, I64, P, P, P]),
+    "pgc_prefill_workspace_bytes": (SZ, [I32]),
+    "pgc_prefill_attn": (I32, [P, P, P, I64, P, I32, I32, F32, P, P, SZ, P]),
+    "pgc_copy_rows": (I32, [P, P, P, P, I64, I64, I64, I64, P]),
+    "pgc_kv_restore_dense": (I32, [P, P, I64, I64, P, P, I64, P, I64, I64, I64, P]),
+    "pgc_kv_snapshot_dense": (I32, [P, P, I64, P, I64, I64, P, P, I64, I64, I64, P]),
+    "pgc_kv_copy_tokens": (I32, [P, P, I64, P, I64, I64, P, P, I64, P, I64, I64, I64, P]),
+    "pgc_copy_regions": (I32, [C.POINTER(Region), I32, P]),
+    "pgc_zero_regions": (I32, [C.POINTER(Region), I32, P]),
+    "pgc_rollback": (I32, [P, P, I32, I32, C.POINTER(Region), I32, P]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads the native library (raises if it is missing: no fallback exists)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is not built; run `python -m peregrine_b200.build` "
+                "(the CUDA library is the only implementation)")
+        handle = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise PgcError(status, what)
+
+
+# ----------------------------------------------------------------------------- host helpers
+
+def full_cache_stride_for_max_seq(max_seq: int) -> int:
+    out = U64(0)
+    check(lib().pgc_full_cache_stride_for_max_seq(max_seq, C.byref(out)),
+          "pgc_full_cache_stride_for_max_seq")
+    return out.value
+
+
+def rope_table(max_pos: int, rot_dim: int = ROTARY_DIM, theta: float = 1e7):
+    import numpy as np
+    t = np.empty((max_pos, rot_dim), dtype=np.float32)
+    check(lib().pgc_rope_table_fill(t.ctypes.data, max_pos, rot_dim, theta), "pgc_rope_table_fill")
+    return t
+
+
+def device_error(clear: bool = True) -> tuple[int, int]:
+    code, detail = I32(0), I64(0)
+    check(lib().pgc_device_error(C.byref(code), C.byref(detail), int(clear)), "pgc_device_error")
+    return code.value, detail.value
+
+
+# ----------------------------------------------------------------------------- torch helpers
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+def decode_workspace_bytes(batch: int, num_queries: int, max_seq_len: int) -> int:
+    return int(lib().pgc_decode_workspace_bytes(batch, num_queries, max_seq_len))
+
+
+def decode_attn(q, k_pages, v_pages, block_tables, seq_lens, max_seq_len, scale, out,
+                workspace, num_queries=1, gate=None, stream=None) -> None:
+    batch = seq_lens.shape[0]
+    check(lib().pgc_decode_attn(
+        _ptr(q), _ptr(k_pages), _ptr(v_pages), k_pages.shape[0], _ptr(block_tables),
+        block_tables.shape[1], _ptr(seq_lens), batch, num_queries, max_seq_len, scale, _ptr(gate),
+        _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(stream)),
+        "pgc_decode_attn")
+
+
+def decode_attn_partials(q, k_pages, v_pages, block_tables, seq_lens, max_seq_len, scale,
+                         partials, workspace, num_queries=1, stream=None) -> None:
+    batch = seq_lens.shape[0]
+    check(lib().pgc_decode_attn_partials(
+        _ptr(q), _ptr(k_pages), _ptr(v_pages), k_pages.shape[0], _ptr(block_tables),
+        block_tables.shape[1], _ptr(seq_lens), batch, num_queries, max_seq_len, scale,
+        _ptr(partials), _ptr(workspace), workspace.numel() * workspace.element_size(),
+        _stream(stream)), "pgc_decode_attn_partials")
+
+
+def merge_partials(partials, rows, num_parts, part_stride, out, gate=None, stream=None) -> None:
+    check(lib().pgc_merge_partials(_ptr(partials), rows, num_parts, part_stride, _ptr(gate),
+                                   _ptr(out), _stream(stream)), "pgc_merge_partials")
+
+
+def append_kv_rope(q_in, q_out, k_in, v_in, rope, positions, slots, k_pages, v_pages,
+                   mode=APPEND_DECODE, gate_out=None, q_norm_w=None, k_norm_w=None,
+                   stream=None) -> None:
+    tokens = positions.shape[0]
+    q_head_stride = q_in.shape[-1]
+    check(lib().pgc_append_kv_rope(
+        _ptr(q_in), q_head_stride, _ptr(q_out), _ptr(gate_out), _ptr(k_in), _ptr(v_in),
+        _ptr(q_norm_w), _ptr(k_norm_w), _ptr(rope), rope.shape[0], _ptr(positions), _ptr(slots),
+        tokens, _ptr(k_pages), _ptr(v_pages), k_pages.shape[0], mode, _stream(stream)),
+        "pgc_append_kv_rope")
+
+
+def prefill_workspace_bytes(chunk_len: int) -> int:
+    return int(lib().pgc_prefill_workspace_bytes(chunk_len))
+
+
+def prefill_attn(q, k_pages, v_pages, block_table, prefix_len, chunk_len, scale, out, workspace,
+                 stream=None) -> None:
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().pgc_prefill_attn(
+        _ptr(q), _ptr(k_pages), _ptr(v_pages), k_pages.shape[0], _ptr(block_table), prefix_len,
+        chunk_len, scale, _ptr(out), _ptr(workspace), ws_bytes, _stream(stream)),
+        "pgc_prefill_attn")
+
+
+def copy_rows(dst, src, n_rows, row_bytes, dst_pitch, src_pitch, dst_rows=None, src_rows=None,
+              stream=None) -> None:
+    d = dst if isinstance(dst, int) else dst.data_ptr()
+    s = src if isinstance(src, int) else src.data_ptr()
+    check(lib().pgc_copy_rows(d, s, _ptr(dst_rows), _ptr(src_rows), n_rows, row_bytes, dst_pitch,
+                              src_pitch, _stream(stream)), "pgc_copy_rows")
+
+
+def kv_restore_dense(k_dense, v_dense, src_stride, src_token, k_pages, v_pages, block_table,
+                     dst_token, count, stream=None) -> None:
+    check(lib().pgc_kv_restore_dense(
+        _ptr(k_dense), _ptr(v_dense), src_stride, src_token, _ptr(k_pages), _ptr(v_pages),
+        k_pages.shape[0], _ptr(block_table), block_table.shape[-1], dst_token, count,
+        _stream(stream)), "pgc_kv_restore_dense")
+
+
+def kv_snapshot_dense(k_pages, v_pages, block_table, src_token, k_dense, v_dense, dst_stride,
+                      dst_token, count, stream=None) -> None:
+    check(lib().pgc_kv_snapshot_dense(
+        _ptr(k_pages), _ptr(v_pages), k_pages.shape[0], _ptr(block_table),
+        block_table.shape[-1], src_token, _ptr(k_dense), _ptr(v_dense), dst_stride, dst_token,
+        count, _stream(stream)), "pgc_kv_snapshot_dense")
+
+
+def kv_copy_tokens(src_k, src_v, src_table, src_token, dst_k, dst_v, dst_table, dst_token, count,
+                   stream=None) -> None:
+    check(lib().pgc_kv_copy_tokens(
+        _ptr(src_k), _ptr(src_v), src_k.shape[0], _ptr(src_table), src_table.shape[-1],
+        src_token, _ptr(dst_k), _ptr(dst_v), dst_k.shape[0], _ptr(dst_table),
+        dst_table.shape[-1], dst_token, count, _stream(stream)), "pgc_kv_copy_tokens")
+
+
+def _regions(pairs):
+    arr = (Region * max(1, len(pairs)))()
+    for i, (dst, src, nbytes) in enumerate(pairs):
+        arr[i].dst = dst if isinstance(dst, int) else dst.data_ptr()
+        arr[i].src = (src if isinstance(src, int) else src.data_ptr()) if src is not None else None
+        arr[i].bytes = nbytes
+    return arr
+
+
+def copy_regions(pairs, stream=None) -> None:
+    """pairs: [(dst, src, nbytes)] with tensors or raw addresses."""
+    check(lib().pgc_copy_regions(_regions(pairs), len(pairs), _stream(stream)), "pgc_copy_regions")
+
+
+def zero_regions(pairs, stream=None) -> None:
+    check(lib().pgc_zero_regions(_regions([(d, None, n) for d, n in pairs]), len(pairs),
+                                 _stream(stream)), "pgc_zero_regions")
+
+
+def rollback(accept, seq_lens, seq_index, reject_tokens, pairs, stream=None) -> None:
+    check(lib().pgc_rollback(_ptr(accept), _ptr(seq_lens), seq_index, reject_tokens,
+                             _regions(pairs), len(pairs), _stream(stream)), "pgc_rollback")

@@ -1,0 +1,266 @@
+// cache_copy.cu — byte-exact cache movement for prefix snapshot/restore, hidden rows, linear
+// state and MTP rollback (sm_100a).
+//
+// The reference does all of this as host memcpy on CPU-visible Metal buffers
+// (src/model/state.zig:124-230, src/server/prefix_state_cache.zig:584-629,
+// src/server/decode_loop.zig:295-311). Here every copy is one kernel launch of 16-byte
+// vector loads/stores, HBM-bound, reading and writing any memory the GPU can address
+// (HBM, or pinned host memory for a host-resident prefix store).
+#include "pgc_common.cuh"
+#include "pgc_internal.h"
+
+namespace pgc {
+
+PGC_DEFINE_ERROR_WORD(g_copy_err);
+
+namespace {
+
+int launch_blocks(int64_t work_items, int threads) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int64_t want = (work_items + threads - 1) / threads;
+    const int64_t cap = (int64_t)sms * 16;
+    if (want > cap) want = cap;
+    if (want < 1) want = 1;
+    return (int)want;
+}
+
+// ---------------------------------------------------------------- row gather / scatter
+template <typename V>
+__global__ void __launch_bounds__(256)
+    copy_rows_kernel(uint8_t *dst, const uint8_t *src, const int32_t *dst_rows,
+                     const int32_t *src_rows, int64_t n_rows, int64_t units_per_row,
+                     int64_t dst_pitch, int64_t src_pitch) {
+    const int64_t total = n_rows * units_per_row;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / units_per_row;
+        const int64_t u = i - r * units_per_row;
+        const int64_t dr = dst_rows ? dst_rows[r] : r;
+        const int64_t sr = src_rows ? src_rows[r] : r;
+        reinterpret_cast<V *>(dst + dr * dst_pitch)[u] =
+            reinterpret_cast<const V *>(src + sr * src_pitch)[u];
+    }
+}
+
+// ---------------------------------------------------------------- dense <-> paged KV
+// Resolves logical token t of a paged sequence to the element offset of its (kvh) row, or -1
+// (recorded) when the table entry or the page id is out of range.
+__device__ __forceinline__ int64_t paged_row(const int32_t *table, int64_t n_table,
+                                             int64_t num_pages, int64_t t, int kvh) {
+    const int64_t pi = t / kPage;
+    if (t < 0 || pi >= n_table) {
+        record_error(&g_copy_err, kErrTableOutOfRange, t);
+        return -1;
+    }
+    const int64_t page = table[pi];
+    if (page < 0 || page >= num_pages) {
+        record_error(&g_copy_err, kErrPageOutOfRange, page);
+        return -1;
+    }
+    return ((page * kNumKvHeads + kvh) * kPage + t % kPage) * kHeadDim;
+}
+
+constexpr int kDenseTile = 32;  // tokens per CTA
+
+// One CTA per (32-token tile, kv head). K rows are 512 B in both layouts (uint4 copies);
+// V is value-dim-major in the dense layout and token-major in the pages, so it is
+// transposed through shared memory: coalesced 64-byte runs on the dense side, whole 512-byte
+// rows on the page side.
+__global__ void __launch_bounds__(256)
+    kv_dense_kernel(bool restore, uint16_t *dk, uint16_t *dv, int64_t dstride, int64_t dtok,
+                    uint16_t *kp, uint16_t *vp, int64_t num_pages, const int32_t *table,
+                    int64_t n_table, int64_t ptok, int64_t count) {
+    __shared__ uint16_t vt[kHeadDim][kDenseTile + 2];
+    __shared__ int64_t rows[kDenseTile];
+    const int kvh = blockIdx.y;
+    const int64_t base = (int64_t)blockIdx.x * kDenseTile;
+    const int n = (int)(count - base < kDenseTile ? count - base : kDenseTile);
+    const int tid = threadIdx.x;
+    if (tid < kDenseTile) rows[tid] = tid < n ? paged_row(table, n_table, num_pages, ptok + base + tid, kvh) : -1;
+    __syncthreads();
+
+    // K: 32 tokens x 32 uint4
+    for (int i = tid; i < n * 32; i += 256) {
+        const int tt = i >> 5, u = i & 31;
+        const int64_t pr = rows[tt];
+        if (pr < 0) continue;
+        uint4 *prow = reinterpret_cast<uint4 *>(kp + pr);
+        uint4 *drow = reinterpret_cast<uint4 *>(dk + ((int64_t)kvh * dstride + dtok + base + tt) * kHeadDim);
+        if (restore) prow[u] = drow[u];
+        else drow[u] = prow[u];
+    }
+    // V
+    if (restore) {
+        for (int i = tid; i < kHeadDim * kDenseTile; i += 256) {
+            const int d = i / kDenseTile, tt = i % kDenseTile;
+            if (tt < n) vt[d][tt] = dv[((int64_t)kvh * kHeadDim + d) * dstride + dtok + base + tt];
+        }
+        __syncthreads();
+        for (int i = tid; i < n * kHeadDim; i += 256) {
+            const int tt = i / kHeadDim, d = i % kHeadDim;
+            const int64_t pr = rows[tt];
+            if (pr >= 0) vp[pr + d] = vt[d][tt];
+        }
+    } else {
+        for (int i = tid; i < n * kHeadDim; i += 256) {
+            const int tt = i / kHeadDim, d = i % kHeadDim;
+            const int64_t pr = rows[tt];
+            vt[d][tt] = pr >= 0 ? vp[pr + d] : 0;
+        }
+        __syncthreads();
+        for (int i = tid; i < kHeadDim * kDenseTile; i += 256) {
+            const int d = i / kDenseTile, tt = i % kDenseTile;
+            if (tt < n && rows[tt] >= 0)
+                dv[((int64_t)kvh * kHeadDim + d) * dstride + dtok + base + tt] = vt[d][tt];
+        }
+    }
+}
+
+// paged -> paged, one warp per (token, kv head): 512 B of K and 512 B of V
+__global__ void __launch_bounds__(256)
+    kv_copy_tokens_kernel(const uint16_t *sk, const uint16_t *sv, int64_t s_pages,
+                          const int32_t *s_table, int64_t s_n, int64_t s_tok, uint16_t *dk,
+                          uint16_t *dv, int64_t d_pages, const int32_t *d_table, int64_t d_n,
+                          int64_t d_tok, int64_t count) {
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= count * kNumKvHeads) return;
+    const int64_t i = gw / kNumKvHeads;
+    const int kvh = (int)(gw % kNumKvHeads);
+    int64_t so = 0, dof = 0;
+    if (lane == 0) {
+        so = paged_row(s_table, s_n, s_pages, s_tok + i, kvh);
+        dof = paged_row(d_table, d_n, d_pages, d_tok + i, kvh);
+    }
+    so = __shfl_sync(0xffffffffu, so, 0);
+    dof = __shfl_sync(0xffffffffu, dof, 0);
+    if (so < 0 || dof < 0) return;
+    reinterpret_cast<uint4 *>(dk + dof)[lane] = reinterpret_cast<const uint4 *>(sk + so)[lane];
+    reinterpret_cast<uint4 *>(dv + dof)[lane] = reinterpret_cast<const uint4 *>(sv + so)[lane];
+}
+
+// ---------------------------------------------------------------- batched regions
+struct RegionTable {
+    uint8_t *dst[PGC_MAX_REGIONS];
+    const uint8_t *src[PGC_MAX_REGIONS];
+    int64_t begin[PGC_MAX_REGIONS + 1];  // prefix sums of units
+    int32_t unit[PGC_MAX_REGIONS];       // 16 (vector) or 1 (byte) bytes per unit
+    int n;
+    int zero;
+    const int32_t *accept;  // rollback: skip everything when *accept != 0
+    int32_t *seq_lens;
+    int seq_index;
+    int reject_tokens;
+};
+
+__global__ void __launch_bounds__(256) regions_kernel(const __grid_constant__ RegionTable rt) {
+    if (rt.accept != nullptr) {
+        if (*rt.accept != 0) return;
+        if (blockIdx.x == 0 && threadIdx.x == 0) rt.seq_lens[rt.seq_index] -= rt.reject_tokens;
+    }
+    const int64_t total = rt.begin[rt.n];
+    int r = 0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        while (i >= rt.begin[r + 1]) ++r;  // i only grows within a thread
+        const int64_t u = i - rt.begin[r];
+        if (rt.unit[r] == 16) {
+            uint4 v = rt.zero ? make_uint4(0, 0, 0, 0) : reinterpret_cast<const uint4 *>(rt.src[r])[u];
+            reinterpret_cast<uint4 *>(rt.dst[r])[u] = v;
+        } else {
+            rt.dst[r][u] = rt.zero ? 0 : rt.src[r][u];
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_copy_rows(void *dst, const void *src, const int32_t *dst_rows,
+                             const int32_t *src_rows, int64_t n_rows, int64_t row_bytes,
+                             int64_t dst_pitch, int64_t src_pitch, cudaStream_t stream) {
+    if (n_rows == 0 || row_bytes == 0) return cudaSuccess;
+    auto aligned = [](int64_t v, int64_t a) { return v % a == 0; };
+    const int64_t ad = (int64_t)(uintptr_t)dst, as = (int64_t)(uintptr_t)src;
+    int vec = 1;
+    if (aligned(ad, 16) && aligned(as, 16) && aligned(row_bytes, 16) && aligned(dst_pitch, 16) &&
+        aligned(src_pitch, 16))
+        vec = 16;
+    else if (aligned(ad, 4) && aligned(as, 4) && aligned(row_bytes, 4) && aligned(dst_pitch, 4) &&
+             aligned(src_pitch, 4))
+        vec = 4;
+    const int64_t upr = row_bytes / vec;
+    const int blocks = launch_blocks(n_rows * upr, 256);
+    uint8_t *d = static_cast<uint8_t *>(dst);
+    const uint8_t *s = static_cast<const uint8_t *>(src);
+    if (vec == 16)
+        copy_rows_kernel<uint4><<<blocks, 256, 0, stream>>>(d, s, dst_rows, src_rows, n_rows, upr, dst_pitch, src_pitch);
+    else if (vec == 4)
+        copy_rows_kernel<uint32_t><<<blocks, 256, 0, stream>>>(d, s, dst_rows, src_rows, n_rows, upr, dst_pitch, src_pitch);
+    else
+        copy_rows_kernel<uint8_t><<<blocks, 256, 0, stream>>>(d, s, dst_rows, src_rows, n_rows, upr, dst_pitch, src_pitch);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_dense(bool restore, uint16_t *dense_k, uint16_t *dense_v,
+                            int64_t dense_stride, int64_t dense_token, uint16_t *k_pages,
+                            uint16_t *v_pages, int64_t num_pages, const int32_t *table,
+                            int64_t n_table, int64_t page_token, int64_t count,
+                            cudaStream_t stream) {
+    if (count == 0) return cudaSuccess;
+    dim3 grid((unsigned)((count + kDenseTile - 1) / kDenseTile), kNumKvHeads);
+    kv_dense_kernel<<<grid, 256, 0, stream>>>(restore, dense_k, dense_v, dense_stride, dense_token,
+                                              k_pages, v_pages, num_pages, table, n_table,
+                                              page_token, count);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_copy_tokens(const uint16_t *sk, const uint16_t *sv, int64_t s_pages,
+                                  const int32_t *s_table, int64_t s_n, int64_t s_tok,
+                                  uint16_t *dk, uint16_t *dv, int64_t d_pages,
+                                  const int32_t *d_table, int64_t d_n, int64_t d_tok,
+                                  int64_t count, cudaStream_t stream) {
+    if (count == 0) return cudaSuccess;
+    const int64_t blocks = (count * kNumKvHeads + 7) / 8;
+    kv_copy_tokens_kernel<<<(unsigned)blocks, 256, 0, stream>>>(sk, sv, s_pages, s_table, s_n, s_tok,
+                                                                dk, dv, d_pages, d_table, d_n, d_tok, count);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_regions(const pgc_region *regions, int n, bool zero, const int32_t *accept,
+                           int32_t *seq_lens, int seq_index, int reject_tokens,
+                           cudaStream_t stream) {
+    RegionTable rt;
+    memset(&rt, 0, sizeof(rt));
+    rt.n = n;
+    rt.zero = zero ? 1 : 0;
+    rt.accept = accept;
+    rt.seq_lens = seq_lens;
+    rt.seq_index = seq_index;
+    rt.reject_tokens = reject_tokens;
+    int64_t acc = 0;
+    for (int i = 0; i < n; ++i) {
+        rt.dst[i] = static_cast<uint8_t *>(regions[i].dst);
+        rt.src[i] = static_cast<const uint8_t *>(regions[i].src);
+        const uintptr_t a = (uintptr_t)regions[i].dst | (zero ? 0 : (uintptr_t)regions[i].src);
+        const bool v16 = (a % 16 == 0) && (regions[i].bytes % 16 == 0);
+        rt.unit[i] = v16 ? 16 : 1;
+        rt.begin[i] = acc;
+        acc += (int64_t)(regions[i].bytes / rt.unit[i]);
+    }
+    rt.begin[n] = acc;
+    if (acc == 0 && accept == nullptr) return cudaSuccess;
+    const int blocks = launch_blocks(acc, 256);
+    regions_kernel<<<blocks, 256, 0, stream>>>(rt);
+    return cudaGetLastError();
+}
+
+cudaError_t copy_read_error(DevErrorHost *e, bool clear) {
+    cudaError_t r = cudaMemcpyFromSymbol(e, g_copy_err, sizeof(DevError));
+    if (r != cudaSuccess || !clear) return r;
+    DevErrorHost z = {0, 0, 0};
+    return cudaMemcpyToSymbol(g_copy_err, &z, sizeof(DevError));
+}
+
+}  // namespace pgc

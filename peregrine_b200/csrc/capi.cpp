@@ -1,0 +1,395 @@
+// capi.cpp — the extern "C" boundary of libperegrine_cuda.so (declared in
+// include/peregrine_cuda.h).
+//
+// Role of the reference's Objective-C bridge (src/runtime/bridge.h:1-103, bridge.m): a flat
+// C ABI that a Zig host binds with @cImport / extern. Each entry validates shapes, bounds and
+// alignment on the host (the reference's kernels only early-return on bad shapes,
+// attention_decode.metal:45-48), resolves per-device state (SM count, cached TMA
+// descriptors) and enqueues the kernels on the caller's stream. No entry allocates device
+// memory: workspaces are caller-owned, as buffers are in the reference (bridge.h:14-16).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "pgc_internal.h"
+
+namespace pgc {
+namespace {
+
+std::mutex g_mu;
+
+struct MapKey {
+    int dev;
+    const void *ptr;
+    int64_t pages;
+    bool operator==(const MapKey &o) const { return dev == o.dev && ptr == o.ptr && pages == o.pages; }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const {
+        return std::hash<const void *>()(k.ptr) ^ (std::hash<int64_t>()(k.pages) * 31) ^ (size_t)k.dev;
+    }
+};
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+int g_sm_count[64] = {0};
+int g_arch_ok[64] = {0};  // 0 unknown, 1 ok, -1 not sm_100
+
+int check_device(int *dev_out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return PGC_ERR_CUDA;
+    if (dev < 0 || dev >= 64) return PGC_ERR_DEVICE;
+    if (g_arch_ok[dev] == 0) {
+        int major = 0, minor = 0, sms = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return PGC_ERR_CUDA;
+        g_sm_count[dev] = sms;
+        g_arch_ok[dev] = (major == 10 && minor == 0) ? 1 : -1;
+    }
+    if (g_arch_ok[dev] != 1) return PGC_ERR_DEVICE;
+    if (dev_out) *dev_out = dev;
+    return PGC_OK;
+}
+
+inline bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? PGC_OK : PGC_ERR_CUDA; }
+
+}  // namespace
+
+int current_sm_count() {
+    int dev = 0;
+    if (check_device(&dev) != PGC_OK) return 148;
+    return g_sm_count[dev];
+}
+
+int pool_tensor_map(const void *pool, int64_t num_pages, CUtensorMap *out) {
+    int dev = 0;
+    int st = check_device(&dev);
+    if (st != PGC_OK) return st;
+    std::lock_guard<std::mutex> lk(g_mu);
+    MapKey key{dev, pool, num_pages};
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+        *out = it->second;
+        return PGC_OK;
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return PGC_ERR_CUDA;
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {(cuuint64_t)PGC_HEAD_DIM, (cuuint64_t)num_pages * 4 * 16};
+    const cuuint64_t strides[1] = {(cuuint64_t)PGC_HEAD_DIM * 2};
+    const cuuint32_t box[2] = {64, 16};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(pool), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return PGC_ERR_CUDA;
+    if (g_maps.size() > 4096) g_maps.clear();
+    g_maps.emplace(key, m);
+    *out = m;
+    return PGC_OK;
+}
+
+}  // namespace pgc
+
+using namespace pgc;
+
+extern "C" {
+
+const char *pgc_status_string(int status) {
+    switch (status) {
+        case PGC_OK: return "ok";
+        case PGC_ERR_INVALID: return "invalid argument";
+        case PGC_ERR_BOUNDS: return "index or length out of bounds";
+        case PGC_ERR_WORKSPACE: return "workspace too small";
+        case PGC_ERR_CUDA: return "CUDA error";
+        case PGC_ERR_ALIGN: return "misaligned pointer or size";
+        case PGC_ERR_DEVICE: return "current device is not sm_100";
+        case PGC_ERR_TIMEOUT: return "bounded device wait timed out";
+        case PGC_ERR_CONTEXT: return "invalid context length";
+        default: return "unknown status";
+    }
+}
+
+int pgc_version(void) { return 100; }
+
+int pgc_device_error(int *code_out, int64_t *detail_out, int clear) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (cudaDeviceSynchronize() != cudaSuccess) return PGC_ERR_CUDA;
+    DevErrorHost e[4] = {};
+    cudaError_t r = decode_read_error(&e[0], clear != 0);
+    if (r == cudaSuccess) r = append_read_error(&e[1], clear != 0);
+    if (r == cudaSuccess) r = copy_read_error(&e[2], clear != 0);
+    if (r != cudaSuccess) return PGC_ERR_CUDA;
+    int code = 0;
+    long long detail = 0;
+    for (int i = 0; i < 4 && code == 0; ++i)
+        if (e[i].code != 0) {
+            code = e[i].code + 100 * i;  // unit in the hundreds digit
+            detail = e[i].detail;
+        }
+    if (code_out) *code_out = code;
+    if (detail_out) *detail_out = detail;
+    return PGC_OK;
+}
+
+int pgc_full_cache_stride_for_max_seq(uint64_t max_seq, uint64_t *stride_out) {
+    if (!stride_out) return PGC_ERR_INVALID;
+    if (max_seq == 0 || max_seq > PGC_MAX_CONTEXT_TOKENS) return PGC_ERR_CONTEXT;
+    const uint64_t a = max_seq >= 16000 ? 64 : 256;
+    const uint64_t r = max_seq % a;
+    *stride_out = r == 0 ? max_seq : max_seq + (a - r);
+    return PGC_OK;
+}
+
+int pgc_rope_table_fill(float *table_host, int64_t max_pos, int rot_dim, double theta) {
+    if (!table_host || max_pos <= 0 || rot_dim <= 0 || (rot_dim & 1) || !(theta > 0.0))
+        return PGC_ERR_INVALID;
+    const int half = rot_dim / 2;
+    for (int64_t p = 0; p < max_pos; ++p)
+        for (int i = 0; i < half; ++i) {
+            const double inv_freq = std::pow(theta, -(2.0 * (double)i) / (double)rot_dim);
+            const double ang = (double)p * inv_freq;
+            table_host[p * rot_dim + i] = (float)std::cos(ang);
+            table_host[p * rot_dim + half + i] = (float)std::sin(ang);
+        }
+    return PGC_OK;
+}
+
+int pgc_append_kv_rope(const uint16_t *q_in, int q_head_stride, uint16_t *q_out,
+                       uint16_t *gate_out, const uint16_t *k_in, const uint16_t *v_in,
+                       const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                       const float *rope_table, int64_t rope_max_pos,
+                       const int32_t *positions, const int64_t *slot_mapping, int64_t tokens,
+                       uint16_t *k_pages, uint16_t *v_pages, int64_t num_pages, int mode,
+                       void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (tokens < 0 || num_pages <= 0 || rope_max_pos <= 0) return PGC_ERR_INVALID;
+    if (mode != PGC_APPEND_DECODE && mode != PGC_APPEND_PREFILL) return PGC_ERR_INVALID;
+    if (q_head_stride != PGC_HEAD_DIM && q_head_stride != 2 * PGC_HEAD_DIM) return PGC_ERR_INVALID;
+    if (gate_out && q_head_stride != 2 * PGC_HEAD_DIM) return PGC_ERR_INVALID;
+    if (tokens == 0) return PGC_OK;
+    if (!q_in || !q_out || !k_in || !v_in || !rope_table || !positions || !slot_mapping ||
+        !k_pages || !v_pages)
+        return PGC_ERR_INVALID;
+    if (!al16(v_in) || !al16(v_pages) || !al16(k_pages)) return PGC_ERR_ALIGN;
+    return cuda_status(launch_append(q_in, q_head_stride, q_out, gate_out, k_in, v_in, q_norm_w,
+                                     k_norm_w, rope_table, rope_max_pos, positions, slot_mapping,
+                                     tokens, k_pages, v_pages, num_pages, mode,
+                                     static_cast<cudaStream_t>(stream)));
+}
+
+size_t pgc_decode_workspace_bytes(int batch, int num_queries, int max_seq_len) {
+    if (batch <= 0 || num_queries <= 0 || max_seq_len <= 0) return 0;
+    return decode_workspace_bytes(batch, num_queries, max_seq_len, current_sm_count());
+}
+
+static int decode_checks(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                         int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
+                         const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
+                         void *workspace, size_t workspace_bytes) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (!q || !k_pages || !v_pages || !block_tables || !seq_lens) return PGC_ERR_INVALID;
+    if (batch <= 0 || num_queries < 1 || num_queries > PGC_MAX_QUERIES || max_seq_len <= 0 ||
+        num_pages <= 0 || max_pages_per_seq <= 0)
+        return PGC_ERR_INVALID;
+    if ((int64_t)max_pages_per_seq * PGC_PAGE_TOKENS < max_seq_len) return PGC_ERR_BOUNDS;
+    if (num_pages * 4 * 16 > INT32_MAX) return PGC_ERR_BOUNDS;  // TMA row coordinate is int32
+    if (!al16(q) || !al16(k_pages) || !al16(v_pages) || !al16(workspace)) return PGC_ERR_ALIGN;
+    if (workspace_bytes < decode_workspace_bytes(batch, num_queries, max_seq_len, current_sm_count()))
+        return PGC_ERR_WORKSPACE;
+    if (!workspace) return PGC_ERR_WORKSPACE;
+    return PGC_OK;
+}
+
+int pgc_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                    int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
+                    const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
+                    float scale, const uint16_t *gate, uint16_t *out, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+    int st = decode_checks(q, k_pages, v_pages, num_pages, block_tables, max_pages_per_seq,
+                           seq_lens, batch, num_queries, max_seq_len, workspace, workspace_bytes);
+    if (st != PGC_OK) return st;
+    if (!out || !std::isfinite(scale)) return PGC_ERR_INVALID;
+    CUtensorMap tk, tv;
+    if ((st = pool_tensor_map(k_pages, num_pages, &tk)) != PGC_OK) return st;
+    if ((st = pool_tensor_map(v_pages, num_pages, &tv)) != PGC_OK) return st;
+    return cuda_status(launch_decode(q, tk, tv, num_pages, block_tables, max_pages_per_seq, seq_lens,
+                                     batch, num_queries, max_seq_len, scale, gate, out, nullptr,
+                                     workspace, current_sm_count(),
+                                     static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_decode_attn_partials(const uint16_t *q, const uint16_t *k_pages,
+                             const uint16_t *v_pages, int64_t num_pages,
+                             const int32_t *block_tables, int max_pages_per_seq,
+                             const int32_t *seq_lens, int batch, int num_queries,
+                             int max_seq_len, float scale, float *partials, void *workspace,
+                             size_t workspace_bytes, void *stream) {
+    int st = decode_checks(q, k_pages, v_pages, num_pages, block_tables, max_pages_per_seq,
+                           seq_lens, batch, num_queries, max_seq_len, workspace, workspace_bytes);
+    if (st != PGC_OK) return st;
+    if (!partials || !std::isfinite(scale)) return PGC_ERR_INVALID;
+    CUtensorMap tk, tv;
+    if ((st = pool_tensor_map(k_pages, num_pages, &tk)) != PGC_OK) return st;
+    if ((st = pool_tensor_map(v_pages, num_pages, &tv)) != PGC_OK) return st;
+    return cuda_status(launch_decode(q, tk, tv, num_pages, block_tables, max_pages_per_seq, seq_lens,
+                                     batch, num_queries, max_seq_len, scale, nullptr, nullptr,
+                                     partials, workspace, current_sm_count(),
+                                     static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_merge_partials(const float *partials, int64_t rows, int num_parts, int64_t part_stride,
+                       const uint16_t *gate, uint16_t *out, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (!partials || !out || rows < 0 || num_parts < 1) return PGC_ERR_INVALID;
+    if (num_parts > 1 && part_stride < rows * PGC_PARTIAL_FLOATS) return PGC_ERR_INVALID;
+    if (rows == 0) return PGC_OK;
+    if (rows > INT32_MAX) return PGC_ERR_BOUNDS;
+    return cuda_status(launch_merge_partials(partials, rows, num_parts, part_stride, gate, out,
+                                             static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_copy_rows(void *dst, const void *src, const int32_t *dst_rows, const int32_t *src_rows,
+                  int64_t n_rows, int64_t row_bytes, int64_t dst_pitch, int64_t src_pitch,
+                  void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (n_rows < 0 || row_bytes < 0 || dst_pitch < 0 || src_pitch < 0) return PGC_ERR_INVALID;
+    if (n_rows == 0 || row_bytes == 0) return PGC_OK;
+    if (!dst || !src) return PGC_ERR_INVALID;
+    if (!dst_rows && row_bytes > dst_pitch && n_rows > 1) return PGC_ERR_INVALID;
+    if (!src_rows && row_bytes > src_pitch && n_rows > 1) return PGC_ERR_INVALID;
+    return cuda_status(launch_copy_rows(dst, src, dst_rows, src_rows, n_rows, row_bytes, dst_pitch,
+                                        src_pitch, static_cast<cudaStream_t>(stream)));
+}
+
+static int dense_checks(const void *kd, const void *vd, int64_t stride, int64_t tok,
+                        const void *kp, const void *vp, int64_t num_pages, const int32_t *table,
+                        int64_t n_table, int64_t ptok, int64_t count) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (count < 0 || stride <= 0 || tok < 0 || ptok < 0 || num_pages <= 0 || n_table < 0)
+        return PGC_ERR_INVALID;
+    if (count == 0) return PGC_OK;
+    if (!kd || !vd || !kp || !vp || !table) return PGC_ERR_INVALID;
+    if (tok + count > stride) return PGC_ERR_BOUNDS;
+    if ((ptok + count + PGC_PAGE_TOKENS - 1) / PGC_PAGE_TOKENS > n_table) return PGC_ERR_BOUNDS;
+    if (!al16(kd) || !al16(kp) || !al16(vp)) return PGC_ERR_ALIGN;
+    return PGC_OK;
+}
+
+int pgc_kv_restore_dense(const uint16_t *k_dense, const uint16_t *v_dense, int64_t src_stride,
+                         int64_t src_token, uint16_t *k_pages, uint16_t *v_pages,
+                         int64_t num_pages, const int32_t *block_table, int64_t n_table,
+                         int64_t dst_token, int64_t count, void *stream) {
+    int st = dense_checks(k_dense, v_dense, src_stride, src_token, k_pages, v_pages, num_pages,
+                          block_table, n_table, dst_token, count);
+    if (st != PGC_OK || count == 0) return st;
+    return cuda_status(launch_kv_dense(true, const_cast<uint16_t *>(k_dense),
+                                       const_cast<uint16_t *>(v_dense), src_stride, src_token,
+                                       k_pages, v_pages, num_pages, block_table, n_table, dst_token,
+                                       count, static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_kv_snapshot_dense(const uint16_t *k_pages, const uint16_t *v_pages, int64_t num_pages,
+                          const int32_t *block_table, int64_t n_table, int64_t src_token,
+                          uint16_t *k_dense, uint16_t *v_dense, int64_t dst_stride,
+                          int64_t dst_token, int64_t count, void *stream) {
+    int st = dense_checks(k_dense, v_dense, dst_stride, dst_token, k_pages, v_pages, num_pages,
+                          block_table, n_table, src_token, count);
+    if (st != PGC_OK || count == 0) return st;
+    return cuda_status(launch_kv_dense(false, k_dense, v_dense, dst_stride, dst_token,
+                                       const_cast<uint16_t *>(k_pages),
+                                       const_cast<uint16_t *>(v_pages), num_pages, block_table,
+                                       n_table, src_token, count, static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_kv_copy_tokens(const uint16_t *src_k_pages, const uint16_t *src_v_pages,
+                       int64_t src_num_pages, const int32_t *src_table, int64_t src_n_table,
+                       int64_t src_token, uint16_t *dst_k_pages, uint16_t *dst_v_pages,
+                       int64_t dst_num_pages, const int32_t *dst_table, int64_t dst_n_table,
+                       int64_t dst_token, int64_t count, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (count < 0 || src_token < 0 || dst_token < 0 || src_num_pages <= 0 || dst_num_pages <= 0)
+        return PGC_ERR_INVALID;
+    if (count == 0) return PGC_OK;
+    if (!src_k_pages || !src_v_pages || !src_table || !dst_k_pages || !dst_v_pages || !dst_table)
+        return PGC_ERR_INVALID;
+    if ((src_token + count + 15) / 16 > src_n_table || (dst_token + count + 15) / 16 > dst_n_table)
+        return PGC_ERR_BOUNDS;
+    if (!al16(src_k_pages) || !al16(src_v_pages) || !al16(dst_k_pages) || !al16(dst_v_pages))
+        return PGC_ERR_ALIGN;
+    return cuda_status(launch_kv_copy_tokens(src_k_pages, src_v_pages, src_num_pages, src_table,
+                                             src_n_table, src_token, dst_k_pages, dst_v_pages,
+                                             dst_num_pages, dst_table, dst_n_table, dst_token,
+                                             count, static_cast<cudaStream_t>(stream)));
+}
+
+static int region_checks(const pgc_region *r, int n, bool need_src) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (n < 0 || n > PGC_MAX_REGIONS) return PGC_ERR_INVALID;
+    if (n > 0 && !r) return PGC_ERR_INVALID;
+    for (int i = 0; i < n; ++i) {
+        if (r[i].bytes == 0) continue;
+        if (!r[i].dst || (need_src && !r[i].src)) return PGC_ERR_INVALID;
+    }
+    return PGC_OK;
+}
+
+int pgc_copy_regions(const pgc_region *regions_host, int n, void *stream) {
+    int st = region_checks(regions_host, n, true);
+    if (st != PGC_OK || n == 0) return st;
+    return cuda_status(launch_regions(regions_host, n, false, nullptr, nullptr, 0, 0,
+                                      static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_zero_regions(const pgc_region *regions_host, int n, void *stream) {
+    int st = region_checks(regions_host, n, false);
+    if (st != PGC_OK || n == 0) return st;
+    return cuda_status(launch_regions(regions_host, n, true, nullptr, nullptr, 0, 0,
+                                      static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_rollback(const int32_t *accept, int32_t *seq_lens, int seq_index, int reject_tokens,
+                 const pgc_region *regions_host, int n, void *stream) {
+    int st = region_checks(regions_host, n, true);
+    if (st != PGC_OK) return st;
+    if (!accept || !seq_lens || seq_index < 0 || reject_tokens < 0) return PGC_ERR_INVALID;
+    return cuda_status(launch_regions(regions_host, n, false, accept, seq_lens, seq_index,
+                                      reject_tokens, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,471 @@
+// decode_attn.cu — split-K flash-decode attention over the paged bf16 KV cache (sm_100a).
+//
+// Behaviour follows sdpa_decode_prefix_flash_partials_bf16 + ..._reduce_gated_bf16
+// (shaders/attention_decode.metal:24-243): per (kv head, context split) the 4 GQA query heads
+// are scored against every token, an online softmax keeps (m, l, o[256]) in fp32, and a
+// log-sum-exp merge combines the splits and applies the optional sigmoid gate.
+//
+// B200 design:
+//   * one CTA per (split, kv head, sequence); 1 producer warp + 4 consumer warps;
+//   * the producer streams each 16-token page of K and V (8 KiB each, contiguous in the pool)
+//     into a 4-stage shared-memory ring with 2-D TMA loads (64 x 16 boxes, 128-byte swizzle,
+//     L2 evict-first), completion on mbarriers;
+//   * consumer warp w takes pages w, w+4, ...; scores and P.V run on the bf16 tensor cores
+//     (mma.m16n8k16, fp32 accumulate) with the query rows (4 heads x up to 4 query tokens) as
+//     the M dimension, so the online softmax stays in registers;
+//   * the 4 warp states are merged in shared memory and each split writes one fp32 partial
+//     per query row; a second small kernel merges splits (and, for context parallelism,
+//     partials gathered from other GPUs).
+#include <cuda.h>
+
+#include "pgc_common.cuh"
+#include "pgc_internal.h"
+
+namespace pgc {
+
+PGC_DEFINE_ERROR_WORD(g_decode_err);
+
+namespace {
+
+constexpr int kConsumers = 4;
+constexpr int kThreads = (kConsumers + 1) * 32;
+constexpr int kStages = 4;
+constexpr int kTileBytes = kPage * kHeadDim * 2;  // one (page, kv head) of K or V: 8 KiB
+constexpr int kStageBytes = 2 * kTileBytes;
+constexpr int kQRowBytes = kHeadDim * 2 + 16;  // padded row: conflict-free ldmatrix
+constexpr int kMinPagesPerSplit = 4;
+constexpr int kMaxPagesPerSplit = 64;
+
+struct SplitParams {
+    const uint16_t *q;
+    const int32_t *block_tables;
+    const int32_t *seq_lens;
+    float *ws;  // [rows][max_splits][258], row = (seq * nq + j) * 16 + head
+    int64_t num_pages;
+    int max_pages_per_seq;
+    int num_queries;
+    int pages_per_split;
+    int max_splits;
+    float scale_log2;
+};
+
+struct SmemLayout {
+    static constexpr int kStageOff = 0;                            // 1024-aligned
+    static constexpr int kQOff = kStageOff + kStages * kStageBytes;  // 65536
+    static constexpr int kMOff = kQOff + 16 * kQRowBytes;
+    static constexpr int kLOff = kMOff + kConsumers * 16 * 4;
+    static constexpr int kBarOff = kLOff + kConsumers * 16 * 4;
+    static constexpr int kBytes = kBarOff + 2 * kStages * 8;
+};
+constexpr int kSmemBytes = SmemLayout::kBytes + 1024;  // + alignment slack
+
+__global__ void __launch_bounds__(kThreads, 2)
+    decode_split_kernel(const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, const SplitParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y;
+    const int seq = blockIdx.z;
+    const int L = p.seq_lens[seq];
+    const int tok_begin = split * p.pages_per_split * kPage;
+    if (tok_begin >= L) return;  // uniform across the CTA
+    const int tok_end = min(L, tok_begin + p.pages_per_split * kPage);
+    const int n_pages = (tok_end - tok_begin + kPage - 1) / kPage;
+    const int nq = p.num_queries;
+    const int nrows = nq * kGroup;
+
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + SmemLayout::kBarOff);
+    uint64_t *empty = full + kStages;
+    uint8_t *q_s = smem + SmemLayout::kQOff;
+    float *m_s = reinterpret_cast<float *>(smem + SmemLayout::kMOff);
+    float *l_s = reinterpret_cast<float *>(smem + SmemLayout::kLOff);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_mbar_init();
+    }
+    // Query rows r = j * 4 + g (query token j, head kvh * 4 + g); rows >= nrows are zero.
+    for (int i = threadIdx.x; i < 16 * (kHeadDim / 8); i += kThreads) {
+        const int r = i / (kHeadDim / 8);
+        const int c = i % (kHeadDim / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < nrows) {
+            const int j = r / kGroup, g = r % kGroup;
+            const uint16_t *src =
+                p.q + ((int64_t)(seq * nq + j) * kNumQHeads + kvh * kGroup + g) * kHeadDim;
+            v = reinterpret_cast<const uint4 *>(src)[c];
+        }
+        *reinterpret_cast<uint4 *>(q_s + r * kQRowBytes + c * 16) = v;
+    }
+    __syncthreads();
+
+    if (warp == kConsumers) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tmk);
+            tma_prefetch_desc(&tmv);
+            const uint64_t pol = l2_policy_evict_first();
+            const int32_t *table =
+                p.block_tables + (int64_t)seq * p.max_pages_per_seq + split * p.pages_per_split;
+            for (int i = 0; i < n_pages; ++i) {
+                const int s = i % kStages;
+                const int round = i / kStages;
+                if (round > 0 && !mbar_wait_bounded(&empty[s], (round - 1) & 1)) {
+                    record_error(&g_decode_err, kErrWaitTimeout, 1);
+                    return;
+                }
+                int page = table[i];
+                if (page < 0 || page >= p.num_pages) {
+                    record_error(&g_decode_err, kErrPageOutOfRange, page);
+                    page = 0;
+                }
+                uint8_t *stage = smem + SmemLayout::kStageOff + s * kStageBytes;
+                mbar_arrive_expect_tx(&full[s], kStageBytes);
+                const int row = (page * kNumKvHeads + kvh) * kPage;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tma_load_2d(stage + c * 2048, &tmk, c * 64, row, &full[s], pol);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    tma_load_2d(stage + kTileBytes + c * 2048, &tmv, c * 64, row, &full[s], pol);
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    const int r0 = lane >> 2;          // C-fragment rows r0 and r0 + 8
+    const int cpair = (lane & 3) * 2;  // C-fragment column pair
+    // visible token bound per C row: query j sees tokens < L - nq + j + 1
+    const int vis0 = (r0 < nrows) ? L - nq + (r0 / kGroup) + 1 : L;
+    const int vis1 = (r0 + 8 < nrows) ? L - nq + ((r0 + 8) / kGroup) + 1 : L;
+
+    float o[32][4];
+#pragma unroll
+    for (int n = 0; n < 32; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    const uint32_t q_base = smem_u32(q_s) + (lane & 15) * kQRowBytes + (lane >> 4) * 16;
+    // ldmatrix lane roles: matrix mi = lane / 8, row-in-matrix = lane % 8
+    const int mi = lane >> 3;
+    const int k_tok = (mi >> 1) * 8 + (lane & 7);  // K: matrices (tok 0-7|8-15) x (k lo|hi)
+    const int k_dim_off = (mi & 1) * 8;
+    const int v_tok = (mi & 1) * 8 + (lane & 7);   // V: matrices (tok lo|hi) x (dim lo|hi)
+    const int v_dim_off = (mi >> 1) * 8;
+
+    bool ok = true;
+    for (int i = warp; i < n_pages; i += kConsumers) {
+        const int s = i % kStages;
+        if (!mbar_wait_bounded(&full[s], (i / kStages) & 1)) {
+            record_error(&g_decode_err, kErrWaitTimeout, 2);
+            ok = false;
+            break;
+        }
+        uint8_t *kt = smem + SmemLayout::kStageOff + s * kStageBytes;
+        uint8_t *vt = kt + kTileBytes;
+        const uint32_t k_base = smem_u32(kt);
+        const uint32_t v_base = smem_u32(vt);
+        const int tok0 = tok_begin + i * kPage;
+        const int nvalid = min(kPage, tok_end - tok0);
+
+        // S[16 rows x 16 tokens] = Q K^T
+        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            ldsm_x4(q_base + kk * 32, a0, a1, a2, a3);
+            ldsm_x4(k_base + swz_page_offset(k_tok, kk * 16 + k_dim_off), b0, b1, b2, b3);
+            mma_bf16_16816(sacc[0], a0, a1, a2, a3, b0, b1);
+            mma_bf16_16816(sacc[1], a0, a1, a2, a3, b2, b3);
+        }
+
+        // masked, log2-scaled scores; online softmax in registers
+        float sc[2][4];
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int t = tok0 + n * 8 + cpair + e;
+                sc[n][e] = (t < vis0) ? sacc[n][e] * p.scale_log2 : -INFINITY;
+                sc[n][2 + e] = (t < vis1) ? sacc[n][2 + e] * p.scale_log2 : -INFINITY;
+                mx0 = fmaxf(mx0, sc[n][e]);
+                mx1 = fmaxf(mx1, sc[n][2 + e]);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float mu0 = (mn0 == -INFINITY) ? 0.f : mn0;
+        const float mu1 = (mn1 == -INFINITY) ? 0.f : mn1;
+        const float corr0 = fast_exp2(m0 - mu0);  // m = -inf -> 0
+        const float corr1 = fast_exp2(m1 - mu1);
+        m0 = mn0;
+        m1 = mn1;
+        float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                sc[n][e] = fast_exp2(sc[n][e] - mu0);
+                sc[n][2 + e] = fast_exp2(sc[n][2 + e] - mu1);
+                ps0 += sc[n][e];
+                ps1 += sc[n][2 + e];
+            }
+        }
+        l0 = l0 * corr0 + ps0;
+        l1 = l1 * corr1 + ps1;
+        if (__any_sync(0xffffffffu, corr0 != 1.f || corr1 != 1.f)) {
+#pragma unroll
+            for (int n = 0; n < 32; ++n) {
+                o[n][0] *= corr0;
+                o[n][1] *= corr0;
+                o[n][2] *= corr1;
+                o[n][3] *= corr1;
+            }
+        }
+        const uint32_t pa0 = pack_bf16x2(sc[0][0], sc[0][1]);
+        const uint32_t pa1 = pack_bf16x2(sc[0][2], sc[0][3]);
+        const uint32_t pa2 = pack_bf16x2(sc[1][0], sc[1][1]);
+        const uint32_t pa3 = pack_bf16x2(sc[1][2], sc[1][3]);
+
+        if (nvalid < kPage) {
+            // Slots past the sequence end hold stale bytes; zero their V rows so that a
+            // NaN pattern cannot leak through a zero probability.
+            for (int idx = lane; idx < (kPage - nvalid) * 4 * 8; idx += 32) {
+                const int row = nvalid + idx / 32;
+                const int unit = idx % 32;  // 4 boxes x 8 units of 16 B
+                *reinterpret_cast<uint4 *>(vt + (unit >> 3) * 2048 + row * 128 + (unit & 7) * 16) =
+                    make_uint4(0, 0, 0, 0);
+            }
+            fence_proxy_async_smem();  // generic writes before any later async-proxy refill
+            __syncwarp();
+        }
+
+        // O[16 x 256] += P[16 x 16] V[16 x 256]
+#pragma unroll
+        for (int nd = 0; nd < 16; ++nd) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_trans(v_base + swz_page_offset(v_tok, nd * 16 + v_dim_off), b0, b1, b2, b3);
+            mma_bf16_16816(o[2 * nd], pa0, pa1, pa2, pa3, b0, b1);
+            mma_bf16_16816(o[2 * nd + 1], pa0, pa1, pa2, pa3, b2, b3);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ---------------------------------------------------------------- merge 4 warp states
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    // all consumers are past their last stage read: reuse the ring as fp32 scratch
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+    float *o_s = reinterpret_cast<float *>(smem + SmemLayout::kStageOff);  // [4][16][256]
+    if ((lane & 3) == 0) {
+        m_s[warp * 16 + r0] = m0;
+        l_s[warp * 16 + r0] = l0;
+        m_s[warp * 16 + r0 + 8] = m1;
+        l_s[warp * 16 + r0 + 8] = l1;
+    }
+    if (r0 < nrows) {
+#pragma unroll
+        for (int n = 0; n < 32; ++n)
+            *reinterpret_cast<float2 *>(&o_s[(warp * 16 + r0) * kHeadDim + n * 8 + cpair]) =
+                make_float2(o[n][0], o[n][1]);
+    }
+    if (r0 + 8 < nrows) {
+#pragma unroll
+        for (int n = 0; n < 32; ++n)
+            *reinterpret_cast<float2 *>(&o_s[(warp * 16 + r0 + 8) * kHeadDim + n * 8 + cpair]) =
+                make_float2(o[n][2], o[n][3]);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+    if (!ok) return;
+
+    const int tid = threadIdx.x;  // 0..127
+    for (int r = 0; r < nrows; ++r) {
+        float ma = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumers; ++w) ma = fmaxf(ma, m_s[w * 16 + r]);
+        float wt[kConsumers];
+        float den = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumers; ++w) {
+            const float mw = m_s[w * 16 + r];
+            wt[w] = (mw == -INFINITY) ? 0.f : fast_exp2(mw - ma);
+            den += l_s[w * 16 + r] * wt[w];
+        }
+        const int j = r / kGroup, g = r % kGroup;
+        const int64_t row = (int64_t)(seq * nq + j) * kNumQHeads + kvh * kGroup + g;
+        float *dst = p.ws + (row * p.max_splits + split) * kPartial;
+        for (int d = tid; d < kHeadDim; d += kConsumers * 32) {
+            float acc = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumers; ++w) acc += o_s[(w * 16 + r) * kHeadDim + d] * wt[w];
+            dst[2 + d] = acc;
+        }
+        if (tid == 0) {
+            dst[0] = (ma == -INFINITY) ? -INFINITY : ma * kLn2;  // natural-log units
+            dst[1] = den;
+        }
+    }
+}
+
+// Log-sum-exp merge of a row's partials (attention_decode.metal:215-243). One CTA per row,
+// one thread per output dim. nparts < 0: derive the part count from the sequence length.
+struct MergeParams {
+    const float *parts;
+    int64_t row_stride;   // floats between rows
+    int64_t part_stride;  // floats between parts of a row
+    int nparts;
+    const int32_t *seq_lens;  // used when nparts < 0
+    int rows_per_seq;
+    int tokens_per_split;
+    const uint16_t *gate;
+    uint16_t *out;      // bf16 output, or
+    float *out_partial; // merged (m, l, o) partial
+};
+
+__global__ void __launch_bounds__(256) merge_kernel(const MergeParams p) {
+    const int64_t row = blockIdx.x;
+    const int d = threadIdx.x;
+    int np = p.nparts;
+    if (np < 0) {
+        const int L = p.seq_lens[row / p.rows_per_seq];
+        np = (L + p.tokens_per_split - 1) / p.tokens_per_split;
+    }
+    const float *base = p.parts + row * p.row_stride;
+    float ma = -INFINITY;
+    for (int c = 0; c < np; ++c) ma = fmaxf(ma, base[c * p.part_stride]);
+    float den = 0.f, acc = 0.f;
+    for (int c = 0; c < np; ++c) {
+        const float *pc = base + c * p.part_stride;
+        const float mc = pc[0];
+        const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - ma) * kLog2e);
+        den += pc[1] * w;
+        acc += pc[2 + d] * w;
+    }
+    if (p.out_partial) {
+        float *dst = p.out_partial + row * kPartial;
+        dst[2 + d] = acc;
+        if (d == 0) {
+            dst[0] = ma;
+            dst[1] = den;
+        }
+        return;
+    }
+    float v = (den == 0.f) ? 0.f : acc / den;
+    if (p.gate) {
+        const float g = bf16_bits_to_f32(p.gate[row * kHeadDim + d]);
+        v = v * (1.0f / (1.0f + expf(-g)));
+    }
+    p.out[row * kHeadDim + d] = f32_to_bf16_bits(v);
+}
+
+}  // namespace
+
+DecodePlan decode_plan(int batch, int max_seq_len, int sm_count) {
+    const int64_t max_pages = (max_seq_len + kPage - 1) / kPage;
+    const int64_t units = (int64_t)batch * kNumKvHeads * max_pages;
+    const int64_t target_ctas = (int64_t)sm_count * 2 * 4;
+    int64_t pps = (units + target_ctas - 1) / target_ctas;
+    if (pps < kMinPagesPerSplit) pps = kMinPagesPerSplit;
+    if (pps > kMaxPagesPerSplit) pps = kMaxPagesPerSplit;
+    DecodePlan plan;
+    plan.pages_per_split = (int)pps;
+    plan.max_splits = (int)((max_pages + pps - 1) / pps);
+    if (plan.max_splits < 1) plan.max_splits = 1;
+    return plan;
+}
+
+size_t decode_workspace_bytes(int batch, int num_queries, int max_seq_len, int sm_count) {
+    const DecodePlan plan = decode_plan(batch, max_seq_len, sm_count);
+    const size_t rows = (size_t)batch * num_queries * kNumQHeads;
+    return rows * plan.max_splits * kPartial * sizeof(float);
+}
+
+cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
+                          int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
+                          const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
+                          float scale, const uint16_t *gate, uint16_t *out, float *partials_out,
+                          void *workspace, int sm_count, cudaStream_t stream) {
+    static bool attr_set[64] = {};  // the attribute is per device context
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(decode_split_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemBytes);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    const DecodePlan plan = decode_plan(batch, max_seq_len, sm_count);
+    SplitParams sp;
+    sp.q = q;
+    sp.block_tables = block_tables;
+    sp.seq_lens = seq_lens;
+    sp.ws = static_cast<float *>(workspace);
+    sp.num_pages = num_pages;
+    sp.max_pages_per_seq = max_pages_per_seq;
+    sp.num_queries = num_queries;
+    sp.pages_per_split = plan.pages_per_split;
+    sp.max_splits = plan.max_splits;
+    sp.scale_log2 = scale * kLog2e;
+    dim3 grid(plan.max_splits, kNumKvHeads, batch);
+    decode_split_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tk, tv, sp);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    MergeParams mp;
+    mp.parts = sp.ws;
+    mp.row_stride = (int64_t)plan.max_splits * kPartial;
+    mp.part_stride = kPartial;
+    mp.nparts = -1;
+    mp.seq_lens = seq_lens;
+    mp.rows_per_seq = num_queries * kNumQHeads;
+    mp.tokens_per_split = plan.pages_per_split * kPage;
+    mp.gate = gate;
+    mp.out = out;
+    mp.out_partial = partials_out;
+    const int64_t rows = (int64_t)batch * num_queries * kNumQHeads;
+    merge_kernel<<<(unsigned)rows, kHeadDim, 0, stream>>>(mp);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_parts,
+                                  int64_t part_stride, const uint16_t *gate, uint16_t *out,
+                                  cudaStream_t stream) {
+    MergeParams mp;
+    mp.parts = partials;
+    mp.row_stride = kPartial;
+    mp.part_stride = part_stride;
+    mp.nparts = num_parts;
+    mp.seq_lens = nullptr;
+    mp.rows_per_seq = 1;
+    mp.tokens_per_split = 1;
+    mp.gate = gate;
+    mp.out = out;
+    mp.out_partial = nullptr;
+    merge_kernel<<<(unsigned)rows, kHeadDim, 0, stream>>>(mp);
+    return cudaGetLastError();
+}
+
+cudaError_t decode_read_error(DevErrorHost *e, bool clear) {
+    cudaError_t r = cudaMemcpyFromSymbol(e, g_decode_err, sizeof(DevError));
+    if (r != cudaSuccess || !clear) return r;
+    DevErrorHost z = {0, 0, 0};
+    return cudaMemcpyToSymbol(g_decode_err, &z, sizeof(DevError));
+}
+
+}  // namespace pgc

@@ -1,0 +1,78 @@
+// pgc_internal.h — host-side launchers shared between the C-ABI layer (capi.cpp) and the
+// kernel translation units. Arguments are validated by capi.cpp before these run.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/peregrine_cuda.h"
+
+namespace pgc {
+
+struct DevErrorHost {
+    int code;
+    int pad;
+    long long detail;
+};
+
+// Tensor map over one paged pool viewed as [num_pages * 4 * 16 rows][256] bf16, 64 x 16 boxes,
+// 128-byte swizzle. Cached per (device, base pointer, num_pages).
+int pool_tensor_map(const void *pool, int64_t num_pages, CUtensorMap *out);
+int current_sm_count();
+
+// decode_attn.cu
+struct DecodePlan {
+    int pages_per_split;
+    int max_splits;
+};
+DecodePlan decode_plan(int batch, int max_seq_len, int sm_count);
+size_t decode_workspace_bytes(int batch, int num_queries, int max_seq_len, int sm_count);
+cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
+                          int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
+                          const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
+                          float scale, const uint16_t *gate, uint16_t *out, float *partials_out,
+                          void *workspace, int sm_count, cudaStream_t stream);
+cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_parts,
+                                  int64_t part_stride, const uint16_t *gate, uint16_t *out,
+                                  cudaStream_t stream);
+cudaError_t decode_read_error(DevErrorHost *e, bool clear);
+
+// kv_append.cu
+cudaError_t launch_append(const uint16_t *q_in, int q_head_stride, uint16_t *q_out,
+                          uint16_t *gate_out, const uint16_t *k_in, const uint16_t *v_in,
+                          const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                          const float *rope_table, int64_t rope_max_pos, const int32_t *positions,
+                          const int64_t *slot_mapping, int64_t tokens, uint16_t *k_pages,
+                          uint16_t *v_pages, int64_t num_pages, int mode, cudaStream_t stream);
+cudaError_t append_read_error(DevErrorHost *e, bool clear);
+
+// cache_copy.cu
+cudaError_t launch_copy_rows(void *dst, const void *src, const int32_t *dst_rows,
+                             const int32_t *src_rows, int64_t n_rows, int64_t row_bytes,
+                             int64_t dst_pitch, int64_t src_pitch, cudaStream_t stream);
+cudaError_t launch_kv_dense(bool restore, uint16_t *dense_k, uint16_t *dense_v,
+                            int64_t dense_stride, int64_t dense_token, uint16_t *k_pages,
+                            uint16_t *v_pages, int64_t num_pages, const int32_t *table,
+                            int64_t n_table, int64_t page_token, int64_t count,
+                            cudaStream_t stream);
+cudaError_t launch_kv_copy_tokens(const uint16_t *sk, const uint16_t *sv, int64_t s_pages,
+                                  const int32_t *s_table, int64_t s_n, int64_t s_tok,
+                                  uint16_t *dk, uint16_t *dv, int64_t d_pages,
+                                  const int32_t *d_table, int64_t d_n, int64_t d_tok,
+                                  int64_t count, cudaStream_t stream);
+cudaError_t launch_regions(const pgc_region *regions, int n, bool zero, const int32_t *accept,
+                           int32_t *seq_lens, int seq_index, int reject_tokens,
+                           cudaStream_t stream);
+cudaError_t copy_read_error(DevErrorHost *e, bool clear);
+
+// prefill_attn.cu
+size_t prefill_workspace_bytes(int chunk_len);
+cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
+                           int64_t num_pages, const int32_t *block_table, int prefix_len,
+                           int chunk_len, float scale, uint16_t *out, void *workspace,
+                           cudaStream_t stream);
+cudaError_t prefill_read_error(DevErrorHost *e, bool clear);
+
+}  // namespace pgc
