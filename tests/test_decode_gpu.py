@@ -60,7 +60,7 @@ def test_ragged_batch(cuda, oracle, nq):
 def test_long_sequences_many_splits(cuda, oracle):
     lens = [20001, 40000, 1111]
     q, kp, vp, table, seq, _ = _case(oracle, lens, seed=9)
-    got = _run(cuda, q, kp, vp, table, seq, 1, max_len=65536)
+    got = _run(cuda, q, kp, vp, table, seq, 1, max_len=table.shape[1] * PAGE)
     ref, _ = oracle.decode_paged(q, kp, vp, table, seq, SCALE)
     assert_attn_close(got, ref)
 
