@@ -161,6 +161,27 @@ int pgc_decode_attn_partials(const uint16_t *q, const uint16_t *k_pages,
                              int max_seq_len, float scale, float *partials, void *workspace,
                              size_t workspace_bytes, void *stream);
 
+/* Size of the fixed scratch array behind pgc_decode_attn_static (16 MiB per GPU). */
+#define PGC_DECODE_STATIC_SCRATCH_BYTES (16u << 20)
+
+/* pgc_decode_attn without a caller workspace, for callers that cannot allocate device memory
+ * at all: code running where cudaMalloc is unavailable or forbidden (a host whose allocator
+ * owns all device memory, a real-time serving loop that bans allocation after start-up, a
+ * plugin that is handed only its input and output buffers). The split partials go to a
+ * file-scope device array of PGC_DECODE_STATIC_SCRATCH_BYTES that every GPU loading the
+ * library keeps until the process exits. Inputs, outputs and their meaning are exactly those
+ * of pgc_decode_attn. Returns PGC_ERR_WORKSPACE when pgc_decode_workspace_bytes(batch,
+ * num_queries, max_seq_len) exceeds the array. The first call on a device resolves the
+ * array's device address (cudaGetSymbolAddress) with that device current: make it before
+ * any stream capture. All calls share the array: calls that overlap on the GPU race. Calls
+ * no cudaMalloc, cudaFree or allocating library routine. This entry point has no counterpart
+ * in the reference. */
+int pgc_decode_attn_static(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                           int64_t num_pages, const int32_t *block_tables,
+                           int max_pages_per_seq, const int32_t *seq_lens, int batch,
+                           int num_queries, int max_seq_len, float scale, const uint16_t *gate,
+                           uint16_t *out, void *stream);
+
 /* Log-sum-exp merge of `num_parts` partials per row: m* = max m_p, w_p = exp(m_p - m*),
  * out = sum w_p o_p / sum w_p l_p, times sigmoid(gate) when gate is non-NULL, rounded to
  * bf16. A part with m = -inf has weight 0. Row r, part p lives at

@@ -62,6 +62,7 @@ SIGNATURES = {
     "pgc_append_kv_rope": (I32, [P, I32, P, P, P, P, P, P, P, I64, P, P, I64, P, P, I64, I32, P]),
     "pgc_decode_workspace_bytes": (SZ, [I32, I32, I32]),
     "pgc_decode_attn": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, P, SZ, P]),
+    "pgc_decode_attn_static": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, P]),
     "pgc_decode_attn_partials": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, SZ, P]),
     "pgc_merge_partials": (I32, [P, I64, I32, I64, P, P, P]),
     "pgc_prefill_workspace_bytes": (SZ, [I32]),
@@ -149,6 +150,16 @@ def decode_attn(q, k_pages, v_pages, block_tables, seq_lens, max_seq_len, scale,
         block_tables.shape[1], _ptr(seq_lens), batch, num_queries, max_seq_len, scale, _ptr(gate),
         _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(stream)),
         "pgc_decode_attn")
+
+
+def decode_attn_static(q, k_pages, v_pages, block_tables, seq_lens, max_seq_len, scale, out,
+                       num_queries=1, gate=None, stream=None) -> None:
+    """pgc_decode_attn_static: same attention, scratch in the library's fixed device array."""
+    batch = seq_lens.shape[0]
+    check(lib().pgc_decode_attn_static(
+        _ptr(q), _ptr(k_pages), _ptr(v_pages), k_pages.shape[0], _ptr(block_tables),
+        block_tables.shape[1], _ptr(seq_lens), batch, num_queries, max_seq_len, scale, _ptr(gate),
+        _ptr(out), _stream(stream)), "pgc_decode_attn_static")
 
 
 def decode_attn_partials(q, k_pages, v_pages, block_tables, seq_lens, max_seq_len, scale,

@@ -249,6 +249,24 @@ int pgc_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *
                                      static_cast<cudaStream_t>(stream)));
 }
 
+int pgc_decode_attn_static(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                           int64_t num_pages, const int32_t *block_tables,
+                           int max_pages_per_seq, const int32_t *seq_lens, int batch,
+                           int num_queries, int max_seq_len, float scale, const uint16_t *gate,
+                           uint16_t *out, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (batch <= 0 || num_queries < 1 || num_queries > PGC_MAX_QUERIES || max_seq_len <= 0)
+        return PGC_ERR_INVALID;
+    const size_t need = decode_workspace_bytes(batch, num_queries, max_seq_len, current_sm_count());
+    if (need > (size_t)PGC_DECODE_STATIC_SCRATCH_BYTES) return PGC_ERR_WORKSPACE;
+    void *scratch = nullptr;
+    if ((st = decode_static_scratch(&scratch)) != PGC_OK) return st;
+    return pgc_decode_attn(q, k_pages, v_pages, num_pages, block_tables, max_pages_per_seq,
+                           seq_lens, batch, num_queries, max_seq_len, scale, gate, out, scratch,
+                           (size_t)PGC_DECODE_STATIC_SCRATCH_BYTES, stream);
+}
+
 int pgc_decode_attn_partials(const uint16_t *q, const uint16_t *k_pages,
                              const uint16_t *v_pages, int64_t num_pages,
                              const int32_t *block_tables, int max_pages_per_seq,

@@ -18,6 +18,8 @@
 //     partials gathered from other GPUs).
 #include <cuda.h>
 
+#include <mutex>
+
 #include "pgc_common.cuh"
 #include "pgc_internal.h"
 
@@ -466,6 +468,38 @@ cudaError_t decode_read_error(DevErrorHost *e, bool clear) {
     if (r != cudaSuccess || !clear) return r;
     DevErrorHost z = {0, 0, 0};
     return cudaMemcpyToSymbol(g_decode_err, &z, sizeof(DevError));
+}
+
+}  // namespace pgc
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free decode entry (pgc_decode_attn_static). For callers that cannot call
+// cudaMalloc at all, the split partials live in this fixed array, which every GPU that loads
+// the library holds until the process exits. Every call shares it and it keeps the last
+// call's contents; nothing in it needs to start at zero, because each call's split kernel
+// writes every partial its merge kernel reads. Two calls that overlap on the GPU (different
+// streams, or different host threads on one device) race on it.
+namespace pgc {
+
+constexpr size_t kStaticScratchBytes = (size_t)PGC_DECODE_STATIC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_decode_static_scratch[kStaticScratchBytes];
+
+int decode_static_scratch(void **ptr_out) {
+    // Host code cannot use the array's name as a device address: resolve it once per device,
+    // with that device current. The first call on a device does this set-up.
+    static std::mutex mu;
+    static void *addr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PGC_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(mu);
+    if (addr[dev] == nullptr) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_decode_static_scratch) != cudaSuccess || p == nullptr)
+            return PGC_ERR_CUDA;
+        addr[dev] = p;
+    }
+    *ptr_out = addr[dev];
+    return PGC_OK;
 }
 
 }  // namespace pgc

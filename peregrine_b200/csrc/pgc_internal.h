@@ -38,6 +38,7 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
                                   int64_t part_stride, const uint16_t *gate, uint16_t *out,
                                   cudaStream_t stream);
 cudaError_t decode_read_error(DevErrorHost *e, bool clear);
+int decode_static_scratch(void **ptr_out);
 
 // kv_append.cu
 cudaError_t launch_append(const uint16_t *q_in, int q_head_stride, uint16_t *q_out,

@@ -1,0 +1,56 @@
+"""pgc_decode_attn_static: the decode entry point for callers that cannot allocate device
+memory (a host whose allocator owns the GPU, a serving loop that forbids allocation after
+start-up, a plugin handed only its input and output buffers). It takes no workspace and keeps
+its split partials in the library's fixed device array. Checked through the C ABI against the
+workspace entry point pgc_decode_attn, within the attention tolerance (2e-2 abs + 1e-2 rel),
+on two calls in a row; shapes beyond the array are rejected. Named to be collected last."""
+import numpy as np
+import pytest
+
+from _util import ATOL, NKV, NQ, D, PAGE, RTOL, bf, dev, host_u16, paged_pools
+
+pytestmark = pytest.mark.gpu
+SCALE = 1.0 / 16
+
+
+def _inputs(oracle, lens, seed, nq):
+    rng = np.random.default_rng(seed)
+    ks = [oracle.normal_bf16(L * NKV * D, seed * 100 + 2 * b).reshape(L, NKV, D) for b, L in enumerate(lens)]
+    vs = [oracle.normal_bf16(L * NKV * D, seed * 100 + 2 * b + 1).reshape(L, NKV, D) for b, L in enumerate(lens)]
+    kp, vp, table = paged_pools(rng, ks, vs, sum((L + PAGE - 1) // PAGE for L in lens) + 3)
+    q = oracle.normal_bf16(len(lens) * nq * NQ * D, seed + 50).reshape(len(lens), nq, NQ, D)
+    g = oracle.normal_bf16(q.size, seed + 51).reshape(q.shape)
+    return [dev(x) for x in (q, kp, vp, table, np.array(lens, np.int32), g)]
+
+
+def test_static_scratch_matches_workspace_entry(cuda, oracle):
+    import torch
+    cases = [([4097], 1, 1), ([3000, 17, 1025, 800], 2, 2)]  # two calls in a row
+    for lens, nq, seed in cases:
+        q, kp, vp, table, seq, g = _inputs(oracle, lens, seed, nq)
+        max_len = max(lens)
+        out_static = torch.full((len(lens), nq, NQ, D), -1, dtype=torch.int16, device="cuda")
+        cuda.decode_attn_static(q, kp, vp, table, seq, max_len, SCALE, out_static,
+                                num_queries=nq, gate=g)
+        ws = torch.empty(cuda.decode_workspace_bytes(len(lens), nq, max_len), dtype=torch.uint8,
+                         device="cuda")
+        out_ws = torch.empty_like(out_static)
+        cuda.decode_attn(q, kp, vp, table, seq, max_len, SCALE, out_ws, ws, num_queries=nq, gate=g)
+        torch.cuda.synchronize()
+        a, b = bf(host_u16(out_static)), bf(host_u16(out_ws))
+        assert np.isfinite(a).all()
+        assert (np.abs(a - b) <= ATOL + RTOL * np.abs(b)).all(), np.abs(a - b).max()
+
+
+def test_static_scratch_rejects_oversize(cuda):
+    import torch
+    from peregrine_b200.capi import PgcError
+    batch, max_len = 64, 65536
+    assert cuda.decode_workspace_bytes(batch, 1, max_len) > 16 << 20
+    q = torch.zeros((batch, 1, NQ, D), dtype=torch.int16, device="cuda")
+    pool = torch.zeros((8, NKV, PAGE, D), dtype=torch.int16, device="cuda")
+    table = torch.zeros((batch, max_len // PAGE), dtype=torch.int32, device="cuda")
+    seq = torch.ones(batch, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    with pytest.raises(PgcError, match="WORKSPACE"):
+        cuda.decode_attn_static(q, pool, pool, table, seq, max_len, SCALE, out)
