@@ -193,6 +193,26 @@ int pgc_merge_partials(const float *partials, int64_t rows, int num_parts,
                        void *stream);
 
 /* ---------------------------------------------------------------------------------------
+ * A5: chunked-prefill causal attention (tcgen05 / TMEM)
+ * ------------------------------------------------------------------------------------- */
+
+size_t pgc_prefill_workspace_bytes(int chunk_len);
+
+/* Causal GQA attention of a `chunk_len`-token chunk of ONE sequence over prefix + chunk:
+ * query t (position prefix_len + t) sees cache tokens [0, prefix_len + t]. The chunk's K/V
+ * must already be in the cache (pgc_append_kv_rope). q [chunk_len][16][256] bf16,
+ * out [chunk_len][16][256] bf16, block_table [ceil((prefix_len+chunk_len)/16)] int32.
+ * Replaces the prefix-aware materialised chain prefill_score_prefix_head_major_bf16 →
+ * prefill_softmax_bf16 → prefill_value_prefix_head_major_value_dim_major_bf16
+ * (shaders/attention.metal:1204-1358, 1413-1461, 1816-1964; dispatched at
+ * src/model/block_attn.zig:633-703) and the non-prefix MLX-GEMM route (block_attn.zig:500-566),
+ * with the mask col <= (n - tokens) + t of attention.metal:1347-1353. */
+int pgc_prefill_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                     int64_t num_pages, const int32_t *block_table, int prefix_len,
+                     int chunk_len, float scale, uint16_t *out, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------------------
  * A6-A9, A11: cache copies (prefix snapshot / restore, hidden rows, state)
  * ------------------------------------------------------------------------------------- */
 

@@ -116,6 +116,36 @@ int pool_tensor_map(const void *pool, int64_t num_pages, CUtensorMap *out) {
     return PGC_OK;
 }
 
+int q_tensor_map(const void *q, int tokens, CUtensorMap *out) {
+    int dev = 0;
+    int st = check_device(&dev);
+    if (st != PGC_OK) return st;
+    std::lock_guard<std::mutex> lk(g_mu);
+    MapKey key{dev, q, -(int64_t)tokens - 1};  // negative: distinct from pool keys
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+        *out = it->second;
+        return PGC_OK;
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return PGC_ERR_CUDA;
+    CUtensorMap m;
+    const cuuint64_t dims[3] = {(cuuint64_t)PGC_HEAD_DIM, (cuuint64_t)PGC_NUM_Q_HEADS,
+                                (cuuint64_t)tokens};
+    const cuuint64_t strides[2] = {(cuuint64_t)PGC_HEAD_DIM * 2,
+                                   (cuuint64_t)PGC_HEAD_DIM * PGC_NUM_Q_HEADS * 2};
+    const cuuint32_t box[3] = {64, 4, 32};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(q), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return PGC_ERR_CUDA;
+    if (g_maps.size() > 4096) g_maps.clear();
+    g_maps.emplace(key, m);
+    *out = m;
+    return PGC_OK;
+}
+
 }  // namespace pgc
 
 using namespace pgc;
@@ -147,6 +177,7 @@ int pgc_device_error(int *code_out, int64_t *detail_out, int clear) {
     cudaError_t r = decode_read_error(&e[0], clear != 0);
     if (r == cudaSuccess) r = append_read_error(&e[1], clear != 0);
     if (r == cudaSuccess) r = copy_read_error(&e[2], clear != 0);
+    if (r == cudaSuccess) r = prefill_read_error(&e[3], clear != 0);
     if (r != cudaSuccess) return PGC_ERR_CUDA;
     int code = 0;
     long long detail = 0;
@@ -296,6 +327,31 @@ int pgc_merge_partials(const float *partials, int64_t rows, int num_parts, int64
     if (rows > INT32_MAX) return PGC_ERR_BOUNDS;
     return cuda_status(launch_merge_partials(partials, rows, num_parts, part_stride, gate, out,
                                              static_cast<cudaStream_t>(stream)));
+}
+
+size_t pgc_prefill_workspace_bytes(int chunk_len) {
+    if (chunk_len <= 0) return 0;
+    return prefill_workspace_bytes(chunk_len);
+}
+
+int pgc_prefill_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                     int64_t num_pages, const int32_t *block_table, int prefix_len,
+                     int chunk_len, float scale, uint16_t *out, void *workspace,
+                     size_t workspace_bytes, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (!q || !k_pages || !v_pages || !block_table || !out) return PGC_ERR_INVALID;
+    if (prefix_len < 0 || chunk_len < 0 || num_pages <= 0 || !std::isfinite(scale))
+        return PGC_ERR_INVALID;
+    if (chunk_len == 0) return PGC_OK;
+    if (num_pages * 4 * 16 > INT32_MAX) return PGC_ERR_BOUNDS;
+    if (!al16(q) || !al16(out) || !al16(k_pages) || !al16(v_pages)) return PGC_ERR_ALIGN;
+    if (workspace_bytes < prefill_workspace_bytes(chunk_len)) return PGC_ERR_WORKSPACE;
+    CUtensorMap tk, tv;
+    if ((st = pool_tensor_map(k_pages, num_pages, &tk)) != PGC_OK) return st;
+    if ((st = pool_tensor_map(v_pages, num_pages, &tv)) != PGC_OK) return st;
+    return cuda_status(launch_prefill(q, tk, tv, num_pages, block_table, prefix_len, chunk_len,
+                                      scale, out, workspace, static_cast<cudaStream_t>(stream)));
 }
 
 int pgc_copy_rows(void *dst, const void *src, const int32_t *dst_rows, const int32_t *src_rows,

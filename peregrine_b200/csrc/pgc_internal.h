@@ -21,6 +21,9 @@ struct DevErrorHost {
 // 128-byte swizzle. Cached per (device, base pointer, num_pages).
 int pool_tensor_map(const void *pool, int64_t num_pages, CUtensorMap *out);
 int current_sm_count();
+// Tensor map over a chunk's queries [tokens][16][256] bf16 viewed as (dim, head, token),
+// 64 x 4 x 32 boxes, 128-byte swizzle. Cached per (device, pointer, tokens).
+int q_tensor_map(const void *q, int tokens, CUtensorMap *out);
 
 // decode_attn.cu
 struct DecodePlan {

@@ -1,0 +1,63 @@
+"""GPU parity of the tcgen05 chunked-prefill attention against the CPU oracle, through the C
+ABI. Tolerance: |gpu - oracle| <= 2e-2 + 1e-2 |oracle| (fp32 oracle)."""
+import numpy as np
+import pytest
+
+from _util import NKV, NQ, D, PAGE, assert_attn_close, dev, host_u16, paged_pools
+
+pytestmark = pytest.mark.gpu
+SCALE = 1.0 / 16
+
+
+def _setup(oracle, P, T, seed, spare=5, nan_tail=False):
+    n = P + T
+    rng = np.random.default_rng(seed)
+    k = oracle.normal_bf16(n * NKV * D, seed * 10 + 1).reshape(n, NKV, D)
+    v = oracle.normal_bf16(n * NKV * D, seed * 10 + 2).reshape(n, NKV, D)
+    kp, vp, table = paged_pools(rng, [k], [v], (n + PAGE - 1) // PAGE + spare)
+    if nan_tail and n % PAGE:
+        kp[table[0, n // PAGE], :, n % PAGE:] = 0x7FC0
+        vp[table[0, n // PAGE], :, n % PAGE:] = 0x7FC0
+    q = oracle.normal_bf16(T * NQ * D, seed * 10 + 3).reshape(T, NQ, D)
+    return q, kp, vp, table[0]
+
+
+def _gpu(cuda, q, kp, vp, table, P, T):
+    import torch
+    out = torch.full((T, NQ, D), -1, dtype=torch.int16, device="cuda")
+    cuda.prefill_attn(dev(q), dev(kp), dev(vp), dev(table), P, T, SCALE, out, None)
+    torch.cuda.synchronize()
+    return host_u16(out)
+
+
+@pytest.mark.parametrize("P,T", [(0, 1), (0, 40), (100, 70), (1000, 33), (777, 129), (64, 64),
+                                 (5, 300)])
+def test_prefill_small(cuda, oracle, P, T):
+    q, kp, vp, table = _setup(oracle, P, T, seed=P + T, nan_tail=True)
+    got = _gpu(cuda, q, kp, vp, table, P, T)
+    ref, _ = oracle.prefill_paged(q, kp, vp, table, P, T, SCALE)
+    assert_attn_close(got, ref)
+
+
+def test_prefill_config2_shape(cuda, oracle):
+    """BASELINE config 2 attention shape: 1600-token chunk over a 24576-token prefix. Rows are
+    sampled: the first and last 4 tokens against the oracle (the oracle restricted to those
+    query positions), and the last token against the decode kernel over the same cache."""
+    import torch
+    P, T = 24576, 1600
+    q, kp, vp, table = _setup(oracle, P, T, seed=2, spare=0)
+    got = _gpu(cuda, q, kp, vp, table, P, T)
+    ref_head, _ = oracle.prefill_paged(np.ascontiguousarray(q[:4]), kp, vp, table, P, 4, SCALE)
+    assert_attn_close(got[:4], ref_head)
+    ref_tail, _ = oracle.prefill_paged(np.ascontiguousarray(q[-4:]), kp, vp, table, P + T - 4, 4, SCALE)
+    assert_attn_close(got[-4:], ref_tail)
+    n = P + T
+    ws = torch.empty(cuda.decode_workspace_bytes(1, 1, n), dtype=torch.uint8, device="cuda")
+    out = torch.empty((1, 1, NQ, D), dtype=torch.int16, device="cuda")
+    cuda.decode_attn(dev(np.ascontiguousarray(q[-1:])), dev(kp), dev(vp), dev(table.reshape(1, -1)),
+                     dev(np.array([n], np.int32)), n, SCALE, out, ws)
+    torch.cuda.synchronize()
+    dec = (host_u16(out).reshape(NQ, D).astype(np.uint32) << 16).view(np.float32)
+    assert_attn_close(got[-1], dec)
+    code, _ = cuda.device_error()
+    assert code == 0
