@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--workload", default="config4", choices=["config4", "small"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 1-3 side figures")
+    ap.add_argument("--only-configs", action="store_true",
+                    help="time only the config 1-3 side figures (profiling aid)")
     return ap.parse_args()
 
 
@@ -211,6 +214,203 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------ other configs
+# BASELINE configs 1-3 are timed in the same run (single GPU, rank 0) and reported under
+# "configs"; the headline line stays config 4.
+
+def _ev_time(fn, iters, warmup=3):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def bench_config1(capi, iters=200):
+    """Config 1: one layer, batch 1, 4096 cached tokens + 1 appended at position 4096 (RoPE on
+    64 dims, no norm), decode over 4097 tokens; output bf16 [16x256]. Timed as direct launches
+    and as a replayed CUDA graph of the same two launches."""
+    import torch
+    bf = torch.bfloat16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    L = 4096
+    pages = (L + 1 + PAGE - 1) // PAGE
+    kp = torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g)
+    vp = torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g)
+    table = torch.arange(pages, dtype=torch.int32, device="cuda").view(1, -1)
+    q_in = torch.randn((1, NQ, D), dtype=bf, device="cuda", generator=g)
+    k_in = torch.randn((1, NKV, D), dtype=bf, device="cuda", generator=g)
+    v_in = torch.randn((1, NKV, D), dtype=bf, device="cuda", generator=g)
+    q = torch.empty_like(q_in)
+    out = torch.empty((1, 1, NQ, D), dtype=bf, device="cuda")
+    rope = torch.from_numpy(capi.rope_table(L + 1)).cuda()
+    pos = torch.tensor([L], dtype=torch.int32, device="cuda")
+    slot = torch.tensor([L], dtype=torch.int64, device="cuda")
+    seq = torch.tensor([L + 1], dtype=torch.int32, device="cuda")
+    ws = torch.empty(capi.decode_workspace_bytes(1, 1, L + 1), dtype=torch.uint8, device="cuda")
+
+    def step(st):
+        capi.append_kv_rope(q_in, q, k_in, v_in, rope, pos, slot, kp, vp, stream=st)
+        capi.decode_attn(q, kp, vp, table, seq, L + 1, SCALE, out, ws, stream=st)
+
+    s = torch.cuda.current_stream()
+    direct = _ev_time(lambda: step(s), iters)
+    graph_ms = None
+    try:
+        gr = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        cap.wait_stream(s)
+        with torch.cuda.graph(gr, stream=cap):
+            step(cap)
+        s.wait_stream(cap)
+        graph_ms = _ev_time(gr.replay, iters)
+    except Exception as e:  # the graph figure is optional
+        print(f"config1 graph capture failed: {e}", file=sys.stderr)
+    nbytes = (L + 1) * KV_BYTES_PER_TOKEN + 3 * NQ * D * 2 + 2 * NKV * D * 2
+    best = direct if graph_ms is None else min(direct, graph_ms)
+    return {"workload": "config1: 1 layer, 4097-token decode + 1 append at pos 4096",
+            "us_per_step": round(direct * 1e3, 2),
+            "us_per_step_graph": None if graph_ms is None else round(graph_ms * 1e3, 2),
+            "GB_s": round(nbytes / (best * 1e-3) / 1e9, 1), "algorithmic_bytes": nbytes}
+
+
+def bench_config2(capi, iters=5):
+    """Config 2: restore of a 24576-token prefix from an HBM prefix store (8 layers of
+    dense-layout K/V into 16-token pages under a random permutation, MTP hidden rows
+    [24576x4096] bf16, 24 gated-delta fp32 states [32x128x128], 24 conv bf16 states [3x8192]),
+    then a 1600-token chunk: K/V append with RMSNorm + RoPE, causal attention over
+    prefix + chunk. The q4 projections are out of scope: the chunk's N(0,1) hidden rows
+    [1600x4096] serve directly as Q."""
+    import torch
+    bf = torch.bfloat16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2)
+    P, T, layers = 24576, 1600, LAYERS
+    n = P + T
+    pages = (n + PAGE - 1) // PAGE
+    stride = capi.full_cache_stride_for_max_seq(P)
+    store_k = [torch.randn((NKV, stride, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+    store_v = [torch.randn((NKV, D, stride), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+    store_h = torch.randn((P, 4096), dtype=bf, device="cuda", generator=g)
+    store_gd = [torch.randn(32 * 128 * 128, device="cuda", generator=g) for _ in range(24)]
+    store_cv = [torch.randn(3 * 8192, dtype=bf, device="cuda", generator=g) for _ in range(24)]
+    kp = [torch.empty((pages, NKV, PAGE, D), dtype=bf, device="cuda") for _ in range(layers)]
+    vp = [torch.empty((pages, NKV, PAGE, D), dtype=bf, device="cuda") for _ in range(layers)]
+    live_h = torch.empty((n, 4096), dtype=bf, device="cuda")
+    live = [torch.empty_like(t) for t in store_gd + store_cv]
+    table = torch.randperm(pages, device="cuda", generator=g).to(torch.int32)
+    hidden = torch.randn((T, NQ, D), dtype=bf, device="cuda", generator=g)
+    k_in = torch.randn((T, NKV, D), dtype=bf, device="cuda", generator=g)
+    v_in = torch.randn((T, NKV, D), dtype=bf, device="cuda", generator=g)
+    qw = torch.randn(D, dtype=bf, device="cuda", generator=g)
+    kw = torch.randn(D, dtype=bf, device="cuda", generator=g)
+    rope = torch.from_numpy(capi.rope_table(n)).cuda()
+    pos = torch.arange(P, n, dtype=torch.int32, device="cuda")
+    slots = table.long()[pos.long() // PAGE] * PAGE + pos.long() % PAGE
+    q = torch.empty_like(hidden)
+    out = torch.empty_like(hidden)
+    regions = [(d, s_, s_.numel() * s_.element_size()) for d, s_ in zip(live, store_gd + store_cv)]
+    s = torch.cuda.current_stream()
+
+    def restore():
+        for l in range(layers):
+            capi.kv_restore_dense(store_k[l], store_v[l], stride, 0, kp[l], vp[l], table, 0, P, stream=s)
+        capi.copy_rows(live_h, store_h, P, 4096 * 2, 4096 * 2, 4096 * 2, stream=s)
+        capi.copy_regions(regions, stream=s)
+
+    def chunk_append():
+        for l in range(layers):
+            capi.append_kv_rope(hidden, q, k_in, v_in, rope, pos, slots, kp[l], vp[l],
+                                mode=capi.APPEND_PREFILL, q_norm_w=qw, k_norm_w=kw, stream=s)
+
+    def prefill():
+        for l in range(layers):
+            capi.prefill_attn(q, kp[l], vp[l], table, P, T, SCALE, out, None, stream=s)
+
+    r_ms = _ev_time(restore, iters)
+    a_ms = _ev_time(chunk_append, iters)
+    p_ms = _ev_time(prefill, iters)
+    restore_bytes = layers * P * KV_BYTES_PER_TOKEN + P * 4096 * 2 + 24 * (32 * 128 * 128 * 4 + 3 * 8192 * 2)
+    flops = layers * 4 * NQ * D * (T * P + T * (T + 1) / 2)
+    append_bytes = layers * T * (NQ * D * 2 * 2 + NKV * D * 2 * 4)
+    return {"workload": "config2: restore 24576-token prefix (8 layers KV + MTP hidden + 24 GD/conv "
+                        "states) from an HBM store, then 1600-token chunk append + causal prefill",
+            "restore_ms": round(r_ms, 3), "restore_bytes": restore_bytes,
+            "restore_GB_s_read_plus_write": round(2 * restore_bytes / (r_ms * 1e-3) / 1e9, 1),
+            "append_ms": round(a_ms, 3), "append_GB_s": round(append_bytes / (a_ms * 1e-3) / 1e9, 1),
+            "prefill_ms": round(p_ms, 3), "prefill_flop": flops,
+            "prefill_TFLOP_s": round(flops / (p_ms * 1e-3) / 1e12, 1)}
+
+
+def bench_config3(capi, iters=10):
+    """Config 3: MTP verify over a 32768-token cache on 8 layers, 2 query tokens (draft + bonus)
+    attending in one pass, state snapshot of 24 gated-delta + conv states before the step, a
+    seeded Bernoulli(0.7) acceptance flag, and on reject the device-side truncation of the last
+    KV row plus bit-exact state restore (pgc_rollback)."""
+    import numpy as np
+    import torch
+    bf = torch.bfloat16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    L, layers = 32768, LAYERS
+    pages = (L + 2 + PAGE - 1) // PAGE
+    kp = [torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+    vp = [torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+    table = torch.randperm(pages, device="cuda", generator=g).to(torch.int32).view(1, -1)
+    live = ([torch.randn(32 * 128 * 128, device="cuda", generator=g) for _ in range(24)]
+            + [torch.randn(3 * 8192, dtype=bf, device="cuda", generator=g) for _ in range(24)])
+    snap = [torch.empty_like(t) for t in live]
+    q_in = [torch.randn((2, NQ, 2 * D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+    k_in = [torch.randn((2, NKV, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+    v_in = [torch.randn((2, NKV, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+    q = torch.empty((2, NQ, D), dtype=bf, device="cuda")
+    gate = torch.empty((2, NQ, D), dtype=bf, device="cuda")
+    out = torch.empty((1, 2, NQ, D), dtype=bf, device="cuda")
+    qw = torch.randn(D, dtype=bf, device="cuda", generator=g)
+    kw = torch.randn(D, dtype=bf, device="cuda", generator=g)
+    rope = torch.from_numpy(capi.rope_table(L + 2)).cuda()
+    pos = torch.tensor([L, L + 1], dtype=torch.int32, device="cuda")
+    slots = table[0].long()[pos.long() // PAGE] * PAGE + pos.long() % PAGE
+    seq = torch.tensor([L + 2], dtype=torch.int32, device="cuda")
+    ws = torch.empty(capi.decode_workspace_bytes(1, 2, L + 2), dtype=torch.uint8, device="cuda")
+    flags = (np.random.default_rng(0).random(4096) < 0.7).astype(np.int32)
+    accept = torch.from_numpy(flags).cuda()
+    nb = [t.numel() * t.element_size() for t in live]
+    snap_regions = list(zip(snap, live, nb))
+    back_regions = list(zip(live, snap, nb))
+    s = torch.cuda.current_stream()
+    counter = {"i": 0}
+
+    def step():
+        i = counter["i"] % len(flags)
+        counter["i"] += 1
+        seq.fill_(L + 2)
+        capi.copy_regions(snap_regions, stream=s)
+        for l in range(layers):
+            capi.append_kv_rope(q_in[l], q, k_in[l], v_in[l], rope, pos, slots, kp[l], vp[l],
+                                gate_out=gate, q_norm_w=qw, k_norm_w=kw, stream=s)
+            capi.decode_attn(q, kp[l], vp[l], table, seq, L + 2, SCALE, out, ws, num_queries=2,
+                             gate=gate, stream=s)
+        capi.rollback(accept[i:i + 1], seq, 0, 1, back_regions, stream=s)
+
+    ms = _ev_time(step, iters)
+    kv = layers * (L + 2) * KV_BYTES_PER_TOKEN
+    state = sum(nb)
+    reject_rate = 1.0 - float(flags.mean())
+    moved = kv + 2 * state + reject_rate * 2 * state  # KV read, snapshot r+w, expected restore r+w
+    return {"workload": "config3: MTP verify, 2 queries over 32768 tokens x 8 layers, state "
+                        "snapshot + device-side Bernoulli(0.7) rollback",
+            "ms_per_verify": round(ms, 3), "kv_bytes": kv, "state_bytes": state,
+            "GB_s": round(moved / (ms * 1e-3) / 1e9, 1)}
+
+
 # ------------------------------------------------------------------------------ GPU arm
 
 def run_ours(args, rank, world, local_rank):
@@ -365,6 +565,12 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": args.steps * layers * 3,
         "clocks": clk,
     }
+    if world == 1 and args.workload == "config4" and not args.no_configs:
+        kpool.clear()
+        vpool.clear()
+        torch.cuda.empty_cache()
+        line["configs"] = {"config1": bench_config1(capi), "config2": bench_config2(capi),
+                           "config3": bench_config3(capi)}
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         gbs, dt, desc = cpu_sample(lens, threads, max_tokens=1 << 30, min_seconds=10.0)
@@ -387,6 +593,13 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    if args.only_configs:
+        import torch
+        from peregrine_b200 import capi
+        torch.cuda.set_device(local_rank)
+        print(json.dumps({"configs": {"config1": bench_config1(capi), "config2": bench_config2(capi),
+                                      "config3": bench_config3(capi)}}), flush=True)
+        return
     try:
         run_ours(args, rank, world, local_rank)
     finally:
