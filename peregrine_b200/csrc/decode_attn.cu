@@ -95,20 +95,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         fence_mbar_init();
     }
-    // Query rows r = j * 4 + g (query token j, head kvh * 4 + g); rows >= nrows are zero.
-    for (int i = threadIdx.x; i < 16 * (kHeadDim / 8); i += kThreads) {
-        const int r = i / (kHeadDim / 8);
-        const int c = i % (kHeadDim / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < nrows) {
-            const int j = r / kGroup, g = r % kGroup;
-            const uint16_t *src =
-                p.q + ((int64_t)(seq * nq + j) * kNumQHeads + kvh * kGroup + g) * kHeadDim;
-            v = reinterpret_cast<const uint4 *>(src)[c];
-        }
-        *reinterpret_cast<uint4 *>(q_s + r * kQRowBytes + c * 16) = v;
-    }
-    __syncthreads();
+    __syncthreads();  // barriers initialised: the producer may start streaming K/V now
 
     if (warp == kConsumers) {
         // ------------------------------------------------------------ producer
@@ -144,6 +131,21 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---------------------------------------------------------------- consumers
+    // Query rows (loaded while the first K/V pages are in flight): r = j * 4 + g (query token j, head kvh * 4 + g); rows >= nrows are zero.
+    for (int i = threadIdx.x; i < 16 * (kHeadDim / 8); i += kConsumers * 32) {
+        const int r = i / (kHeadDim / 8);
+        const int c = i % (kHeadDim / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < nrows) {
+            const int j = r / kGroup, g = r % kGroup;
+            const uint16_t *src =
+                p.q + ((int64_t)(seq * nq + j) * kNumQHeads + kvh * kGroup + g) * kHeadDim;
+            v = reinterpret_cast<const uint4 *>(src)[c];
+        }
+        *reinterpret_cast<uint4 *>(q_s + r * kQRowBytes + c * 16) = v;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+
     const int r0 = lane >> 2;          // C-fragment rows r0 and r0 + 8
     const int cpair = (lane & 3) * 2;  // C-fragment column pair
     // visible token bound per C row: query j sees tokens < L - nq + j + 1
@@ -324,8 +326,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 }
 
-// Log-sum-exp merge of a row's partials (attention_decode.metal:215-243). One CTA per row,
-// one thread per output dim. nparts < 0: derive the part count from the sequence length.
+// Log-sum-exp merge of a row's partials (attention_decode.metal:215-243). One CTA per
+// (row, 32-dim chunk): lane = dim, so every partial row read is a coalesced 128-byte run, and
+// the 8 warps take every 8th partial, so the reads of different partials are independent and
+// overlap instead of forming one serial chain. nparts < 0: derive the part count from the
+// sequence length.
 struct MergeParams {
     const float *parts;
     int64_t row_stride;   // floats between rows
@@ -339,9 +344,16 @@ struct MergeParams {
     float *out_partial; // merged (m, l, o) partial
 };
 
-__global__ void __launch_bounds__(256) merge_kernel(const MergeParams p) {
+constexpr int kMergeWarps = 8;
+
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergeParams p) {
+    __shared__ float red_m[kMergeWarps];
+    __shared__ float red_acc[kMergeWarps][32];
+    __shared__ float red_den[kMergeWarps];
     const int64_t row = blockIdx.x;
-    const int d = threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int d = blockIdx.y * 32 + lane;
     int np = p.nparts;
     if (np < 0) {
         const int L = p.seq_lens[row / p.rows_per_seq];
@@ -349,19 +361,38 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams p) {
     }
     const float *base = p.parts + row * p.row_stride;
     float ma = -INFINITY;
-    for (int c = 0; c < np; ++c) ma = fmaxf(ma, base[c * p.part_stride]);
+    for (int c = threadIdx.x; c < np; c += kMergeWarps * 32) ma = fmaxf(ma, base[c * p.part_stride]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+    if (lane == 0) red_m[warp] = ma;
+    __syncthreads();
+    ma = red_m[0];
+#pragma unroll
+    for (int w = 1; w < kMergeWarps; ++w) ma = fmaxf(ma, red_m[w]);
     float den = 0.f, acc = 0.f;
-    for (int c = 0; c < np; ++c) {
+#pragma unroll 4
+    for (int c = warp; c < np; c += kMergeWarps) {
         const float *pc = base + c * p.part_stride;
         const float mc = pc[0];
         const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - ma) * kLog2e);
         den += pc[1] * w;
         acc += pc[2 + d] * w;
     }
+    red_acc[warp][lane] = acc;
+    if (lane == 0) red_den[warp] = den;
+    __syncthreads();
+    if (warp != 0) return;
+    acc = 0.f;
+    den = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) {
+        acc += red_acc[w][lane];
+        den += red_den[w];
+    }
     if (p.out_partial) {
         float *dst = p.out_partial + row * kPartial;
         dst[2 + d] = acc;
-        if (d == 0) {
+        if (blockIdx.y == 0 && lane == 0) {
             dst[0] = ma;
             dst[1] = den;
         }
@@ -441,7 +472,7 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
     mp.out = out;
     mp.out_partial = partials_out;
     const int64_t rows = (int64_t)batch * num_queries * kNumQHeads;
-    merge_kernel<<<(unsigned)rows, kHeadDim, 0, stream>>>(mp);
+    merge_kernel<<<dim3((unsigned)rows, kHeadDim / 32), kMergeWarps * 32, 0, stream>>>(mp);
     return cudaGetLastError();
 }
 
@@ -459,7 +490,7 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
     mp.gate = gate;
     mp.out = out;
     mp.out_partial = nullptr;
-    merge_kernel<<<(unsigned)rows, kHeadDim, 0, stream>>>(mp);
+    merge_kernel<<<dim3((unsigned)rows, kHeadDim / 32), kMergeWarps * 32, 0, stream>>>(mp);
     return cudaGetLastError();
 }
 

@@ -11,11 +11,14 @@
 //
 // CTA = one kv head x 32 query tokens. The 4 GQA heads of the kv head are stacked into the
 // MMA's M = 128 rows (row r = token r/4, head r%4), so every K/V tile is loaded once for 4
-// heads. Warp roles (192 threads):
+// heads. Warp roles (224 threads):
 //   warps 0-3  softmax + epilogue, thread r owns accumulator row r (TMEM lane r);
-//   warp 4     MMA issuer (one elected lane): S = Q K^T (M128 N64 K256), O += P V (M128 N256);
-//   warp 5     TMA producer: Q once, then K/V tiles of 64 keys (4 pages) into a 2-stage ring.
-// TMEM: S at columns [0, 64), O at [128, 384) of a 512-column allocation.
+//   warp 4     MMA issuer (one lane): S = Q K^T (M128 N64 K256), O += P V (M128 N256);
+//   warp 5     TMA producer of Q and of the K tiles (64 keys = 4 pages) into a 2-slot ring;
+//   warp 6     TMA producer of the V tiles into their own 2-slot ring.
+// S and P are double-buffered (TMEM S columns [0,64) and [64,128), O at [128,384) of a
+// 512-column allocation; two P tiles in shared memory), so the tensor core computes S(j+2) and
+// P.V(j) while the softmax warps turn S(j+1) into probabilities.
 #include <cuda.h>
 
 #include "pgc_common.cuh"
@@ -30,7 +33,7 @@ namespace {
 constexpr int kBM = 128;           // rows = 32 tokens x 4 heads
 constexpr int kTokTile = 32;
 constexpr int kBN = 64;            // keys per tile (4 pages)
-constexpr int kThreadsP = 192;
+constexpr int kThreadsP = 224;
 constexpr int kQBytes = kBM * kHeadDim * 2;      // 64 KiB: [4 dim blocks][128 rows][128 B]
 constexpr int kKVTileBytes = kBN * kHeadDim * 2;  // 32 KiB: [4 dim blocks][64 keys][128 B]
 constexpr int kPBytes = kBM * kBN * 2;            // 16 KiB: [128 rows][128 B]
@@ -42,12 +45,12 @@ constexpr float kLazyRescale = 8.0f;  // log2 units: rescale O only when the max
 
 struct SmemP {
     static constexpr int kQ = 0;
-    static constexpr int kK = kQ + kQBytes;
-    static constexpr int kV = kK + kStagesP * kKVTileBytes;
-    static constexpr int kP = kV + kStagesP * kKVTileBytes;
-    static constexpr int kBar = kP + kPBytes;
-    // barriers: q_full, kv_full[2], kv_empty[2], s_full, p_full, p_free
-    static constexpr int kNumBars = 8;
+    static constexpr int kK = kQ + kQBytes;                   // K ring [2]
+    static constexpr int kV = kK + kStagesP * kKVTileBytes;   // V ring [2]
+    static constexpr int kP = kV + kStagesP * kKVTileBytes;   // P [2]
+    static constexpr int kBar = kP + 2 * kPBytes;
+    // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], p_free[2]
+    static constexpr int kNumBars = 15;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kBytes = kTmemSlot + 16;
 };
@@ -189,11 +192,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SmemP::kBar);
     uint64_t *q_full = bars + 0;
-    uint64_t *kv_full = bars + 1;   // [2]
-    uint64_t *kv_empty = bars + 3;  // [2]
-    uint64_t *s_full = bars + 5;
-    uint64_t *p_full = bars + 6;
-    uint64_t *p_free = bars + 7;
+    uint64_t *k_full = bars + 1;   // [2]
+    uint64_t *k_empty = bars + 3;  // [2]
+    uint64_t *v_full = bars + 5;   // [2]
+    uint64_t *v_empty = bars + 7;  // [2]
+    uint64_t *s_full = bars + 9;   // [2] S buffer b holds a finished S tile
+    uint64_t *p_full = bars + 11;  // [2] P buffer b written (128 arrivals)
+    uint64_t *p_free = bars + 13;  // [2] P.V that read P buffer b has completed
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SmemP::kTmemSlot);
     volatile int *abort_flag = &abort_flag_s;
 
@@ -202,13 +207,15 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     if (threadIdx.x == 0) {
         abort_flag_s = 0;
         mbar_init(q_full, 1);
-        for (int s = 0; s < kStagesP; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&k_full[b], 1);
+            mbar_init(&k_empty[b], 1);
+            mbar_init(&v_full[b], 1);
+            mbar_init(&v_empty[b], 1);
+            mbar_init(&s_full[b], 1);
+            mbar_init(&p_full[b], kBM);
+            mbar_init(&p_free[b], 1);
         }
-        mbar_init(s_full, 1);
-        mbar_init(p_full, kBM);
-        mbar_init(p_free, 1);
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -222,28 +229,34 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     uint8_t *q_s = smem + SmemP::kQ;
-    uint8_t *p_s = smem + SmemP::kP;
 
-    if (warp == 5) {
-        // ------------------------------------------------------------ TMA producer
+    if (warp == 5 || warp == 6) {
+        // ------------------------------------------------------------ TMA producers
+        // warp 5 streams Q and the K tiles, warp 6 the V tiles; each ring slot is refilled as
+        // soon as the MMA that read it has completed (S for K, P.V for V).
         if (lane == 0) {
-            tma_prefetch_desc(&tmq);
-            tma_prefetch_desc(&tmk);
-            tma_prefetch_desc(&tmv);
+            const bool is_k = warp == 5;
+            const CUtensorMap *tm = is_k ? &tmk : &tmv;
+            tma_prefetch_desc(tm);
             const uint64_t pol = l2_policy_evict_first();
-            mbar_arrive_expect_tx(q_full, kQBytes);
-            for (int c = 0; c < 4; ++c)
-                tma_load_3d(q_s + c * (kBM * 128), &tmq, c * 64, kvh * kGroup, tok0, q_full);
+            if (is_k) {
+                tma_prefetch_desc(&tmq);
+                mbar_arrive_expect_tx(q_full, kQBytes);
+                for (int c = 0; c < 4; ++c)
+                    tma_load_3d(q_s + c * (kBM * 128), &tmq, c * 64, kvh * kGroup, tok0, q_full);
+            }
+            uint64_t *full = is_k ? k_full : v_full;
+            uint64_t *empty = is_k ? k_empty : v_empty;
+            uint8_t *ring = smem + (is_k ? SmemP::kK : SmemP::kV);
             for (int j = 0; j < n_tiles; ++j) {
-                const int s = j & 1;
-                if (j >= 2 && !wait_or_abort(&kv_empty[s], ((j >> 1) - 1) & 1, abort_flag, 1)) break;
+                const int b = j & 1;
+                if (j >= 2 && !wait_or_abort(&empty[b], ((j >> 1) - 1) & 1, abort_flag, 1)) break;
                 const int key0 = j * kBN;
                 int npg = 0;
                 for (int pp = 0; pp < kBN / kPage; ++pp)
                     if (key0 + pp * kPage < total_keys) ++npg;
-                mbar_arrive_expect_tx(&kv_full[s], (uint32_t)npg * 2 * kPage * kHeadDim * 2);
-                uint8_t *kt = smem + SmemP::kK + s * kKVTileBytes;
-                uint8_t *vt = smem + SmemP::kV + s * kKVTileBytes;
+                mbar_arrive_expect_tx(&full[b], (uint32_t)npg * kPage * kHeadDim * 2);
+                uint8_t *tile = ring + b * kKVTileBytes;
                 for (int pp = 0; pp < npg; ++pp) {
                     int page = p.block_table[(key0 >> 4) + pp];
                     if (page < 0 || page >= p.num_pages) {
@@ -251,53 +264,56 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                         page = 0;
                     }
                     const int row = (page * kNumKvHeads + kvh) * kPage;
-                    for (int c = 0; c < 4; ++c) {
-                        tma_load_2d(kt + c * (kBN * 128) + pp * 2048, &tmk, c * 64, row, &kv_full[s], pol);
-                        tma_load_2d(vt + c * (kBN * 128) + pp * 2048, &tmv, c * 64, row, &kv_full[s], pol);
-                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        tma_load_2d(tile + c * (kBN * 128) + pp * 2048, tm, c * 64, row, &full[b], pol);
                 }
             }
         }
     } else if (warp == 4) {
         // ------------------------------------------------------------ MMA issuer
+        // Issue order S0 S1 PV0 S2 PV1 S3 ...: S(j+2) and P.V(j) run while the softmax
+        // warps work on S(j+1).
         if (lane == 0) {
             constexpr uint32_t idesc_s = umma_idesc(kBM, kBN, false, false);
             constexpr uint32_t idesc_o = umma_idesc(kBM, kHeadDim, false, true);
             const uint32_t q_addr = smem_u32(q_s);
-            const uint32_t p_addr = smem_u32(p_s);
+            auto issue_s = [&](int jj) -> bool {
+                const int b = jj & 1;
+                if (!wait_or_abort(&k_full[b], (jj >> 1) & 1, abort_flag, 3)) return false;
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(smem + SmemP::kK + b * kKVTileBytes);
+#pragma unroll
+                for (int kk = 0; kk < kHeadDim / 16; ++kk)
+                    umma_f16(tmem + kTmemS + b * kBN,
+                             umma_desc(q_addr + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024),
+                             umma_desc(k_addr + (kk >> 2) * (kBN * 128) + (kk & 3) * 32, 16, 1024),
+                             idesc_s, kk > 0 ? 1u : 0u);
+                umma_commit(&k_empty[b]);
+                umma_commit(&s_full[b]);
+                return true;
+            };
             bool ok = wait_or_abort(q_full, 0, abort_flag, 2);
-            auto issue_pv = [&](int jj) {
-                const int ss = jj & 1;
-                const uint32_t v_addr = smem_u32(smem + SmemP::kV + ss * kKVTileBytes);
+            if (ok) ok = issue_s(0);
+            if (ok && n_tiles > 1) ok = issue_s(1);
+            for (int j = 0; ok && j < n_tiles; ++j) {
+                const int b = j & 1;
+                if (!wait_or_abort(&p_full[b], (j >> 1) & 1, abort_flag, 4) ||
+                    !wait_or_abort(&v_full[b], (j >> 1) & 1, abort_flag, 5)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t p_addr = smem_u32(smem + SmemP::kP + b * kPBytes);
+                const uint32_t v_addr = smem_u32(smem + SmemP::kV + b * kKVTileBytes);
 #pragma unroll
                 for (int kk = 0; kk < kBN / 16; ++kk)
                     umma_f16(tmem + kTmemO, umma_desc(p_addr + kk * 32, 16, 1024),
                              umma_desc(v_addr + kk * 2048, kBN * 128, 1024), idesc_o,
-                             (jj > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&kv_empty[ss]);
-                umma_commit(p_free);
-            };
-            for (int j = 0; ok && j < n_tiles; ++j) {
-                const int s = j & 1;
-                if (!wait_or_abort(&kv_full[s], (j >> 1) & 1, abort_flag, 3)) { ok = false; break; }
-                tc_fence_after();
-                if (j > 0) {
-                    if (!wait_or_abort(p_full, (j - 1) & 1, abort_flag, 4)) { ok = false; break; }
-                    tc_fence_after();
-                    issue_pv(j - 1);
-                }
-                const uint32_t k_addr = smem_u32(smem + SmemP::kK + s * kKVTileBytes);
-#pragma unroll
-                for (int kk = 0; kk < kHeadDim / 16; ++kk)
-                    umma_f16(tmem + kTmemS,
-                             umma_desc(q_addr + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024),
-                             umma_desc(k_addr + (kk >> 2) * (kBN * 128) + (kk & 3) * 32, 16, 1024),
-                             idesc_s, kk > 0 ? 1u : 0u);
-                umma_commit(s_full);
-            }
-            if (ok && wait_or_abort(p_full, (n_tiles - 1) & 1, abort_flag, 5)) {
-                tc_fence_after();
-                issue_pv(n_tiles - 1);
+                             (j > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&v_empty[b]);
+                umma_commit(&p_free[b]);
+                if (j + 2 < n_tiles) ok = issue_s(j + 2);
             }
         }
     } else {
@@ -311,45 +327,38 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
-            if (!wait_or_abort(s_full, j & 1, abort_flag, 6)) { ok = false; break; }
+            const int b = j & 1;
+            if (!wait_or_abort(&s_full[b], (j >> 1) & 1, abort_flag, 6)) { ok = false; break; }
             tc_fence_after();
             float sv[64];
             {
-                float a[32], b[32];
-                tmem_ld32(tmem + lane_addr + kTmemS, a);
-                tmem_ld32(tmem + lane_addr + kTmemS + 32, b);
+                float a[32], c2[32];
+                tmem_ld32(tmem + lane_addr + kTmemS + b * kBN, a);
+                tmem_ld32(tmem + lane_addr + kTmemS + b * kBN + 32, c2);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) { sv[i] = a[i]; sv[32 + i] = b[i]; }
+                for (int i = 0; i < 32; ++i) { sv[i] = a[i]; sv[32 + i] = c2[i]; }
             }
             const int key0 = j * kBN;
             float mx = -INFINITY;
+            if (key0 + kBN - 1 <= vis && row_ok) {  // tile entirely visible: no per-key test
 #pragma unroll
-            for (int i = 0; i < kBN; ++i) {
-                sv[i] = (row_ok && key0 + i <= vis) ? sv[i] * p.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, sv[i]);
+                for (int i = 0; i < kBN; ++i) {
+                    sv[i] *= p.scale_log2;
+                    mx = fmaxf(mx, sv[i]);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < kBN; ++i) {
+                    sv[i] = (row_ok && key0 + i <= vis) ? sv[i] * p.scale_log2 : -INFINITY;
+                    mx = fmaxf(mx, sv[i]);
+                }
             }
             const float m_new = fmaxf(m, mx);
             float corr = 1.f;
             if (m_new > m + kLazyRescale) {  // also true the first time a row sees a key
                 corr = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
                 m = m_new;
-            }
-            if (j > 0) {
-                if (!wait_or_abort(p_free, (j - 1) & 1, abort_flag, 7)) { ok = false; break; }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, corr != 1.f)) {
-#pragma unroll 1
-                    for (int cc = 0; cc < kHeadDim / 32; ++cc) {
-                        float o[32];
-                        tmem_ld32(tmem + lane_addr + kTmemO + cc * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= corr;
-                        tmem_st32(tmem + lane_addr + kTmemO + cc * 32, o);
-                    }
-                    tmem_wait_st();
-                }
             }
             const float m_use = (m == -INFINITY) ? 0.f : m;
             float ps = 0.f;
@@ -359,6 +368,30 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                 ps += sv[i];
             }
             l = l * corr + ps;
+            if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+                // O must be stable: wait for P.V(j-1), the last MMA writing it
+                if (!wait_or_abort(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 7)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int cc = 0; cc < kHeadDim / 32; ++cc) {
+                    float o[32];
+                    tmem_ld32(tmem + lane_addr + kTmemO + cc * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= corr;
+                    tmem_st32(tmem + lane_addr + kTmemO + cc * 32, o);
+                }
+                tmem_wait_st();
+            }
+            // P buffer b is free once P.V(j-2), the previous reader, has completed
+            if (j >= 2 && !wait_or_abort(&p_free[b], ((j >> 1) - 1) & 1, abort_flag, 10)) {
+                ok = false;
+                break;
+            }
+            uint8_t *p_s = smem + SmemP::kP + b * kPBytes;
 #pragma unroll
             for (int ch = 0; ch < kBN / 8; ++ch) {
                 uint4 v;
@@ -371,9 +404,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             if (key0 + kBN > total_keys) {
                 // Keys past the cache end (stale slots, or pages not loaded) get zero V rows so
                 // that a NaN pattern cannot reach the P.V product through a zero probability.
-                const int s = j & 1;
-                if (!wait_or_abort(&kv_full[s], (j >> 1) & 1, abort_flag, 8)) { ok = false; break; }
-                uint8_t *vt = smem + SmemP::kV + s * kKVTileBytes;
+                if (!wait_or_abort(&v_full[b], (j >> 1) & 1, abort_flag, 8)) { ok = false; break; }
+                uint8_t *vt = smem + SmemP::kV + b * kKVTileBytes;
                 const int first = total_keys - key0;
                 const int nz = (kBN - first) * 4 * 8;  // rows x 4 dim blocks x 8 units of 16 B
                 for (int i = r; i < nz; i += kBM) {
@@ -385,9 +417,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             }
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[b]);
         }
-        if (ok && wait_or_abort(p_free, (n_tiles - 1) & 1, abort_flag, 9)) {
+        const int jl = n_tiles - 1;
+        if (ok && wait_or_abort(&p_free[jl & 1], (jl >> 1) & 1, abort_flag, 9)) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
             uint16_t *dst = p.out + ((int64_t)t * kNumQHeads + kvh * kGroup + g) * kHeadDim;
