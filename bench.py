@@ -330,9 +330,12 @@ def bench_config2(capi, iters=5):
             capi.append_kv_rope(hidden, q, k_in, v_in, rope, pos, slots, kp[l], vp[l],
                                 mode=capi.APPEND_PREFILL, q_norm_w=qw, k_norm_w=kw, stream=s)
 
+    pws_bytes = capi.prefill_workspace_bytes(P, T)
+    pws = torch.empty(max(pws_bytes, 16), dtype=torch.uint8, device="cuda")
+
     def prefill():
         for l in range(layers):
-            capi.prefill_attn(q, kp[l], vp[l], table, P, T, SCALE, out, None, stream=s)
+            capi.prefill_attn(q, kp[l], vp[l], table, P, T, SCALE, out, pws, stream=s)
 
     r_ms = _ev_time(restore, iters)
     a_ms = _ev_time(chunk_append, iters)

@@ -196,7 +196,9 @@ int pgc_merge_partials(const float *partials, int64_t rows, int num_parts,
  * A5: chunked-prefill causal attention (tcgen05 / TMEM)
  * ------------------------------------------------------------------------------------- */
 
-size_t pgc_prefill_workspace_bytes(int chunk_len);
+/* Workspace bytes pgc_prefill_attn needs for this shape (0 when the grid fills whole waves of
+ * SMs without splitting the key range; otherwise the fp32 partials of the key splits). */
+size_t pgc_prefill_workspace_bytes(int prefix_len, int chunk_len);
 
 /* Causal GQA attention of a `chunk_len`-token chunk of ONE sequence over prefix + chunk:
  * query t (position prefix_len + t) sees cache tokens [0, prefix_len + t]. The chunk's K/V

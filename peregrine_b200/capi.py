@@ -65,7 +65,7 @@ SIGNATURES = {
     "pgc_decode_attn_static": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, P]),
     "pgc_decode_attn_partials": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, SZ, P]),
     "pgc_merge_partials": (I32, [P, I64, I32, I64, P, P, P]),
-    "pgc_prefill_workspace_bytes": (SZ, [I32]),
+    "pgc_prefill_workspace_bytes": (SZ, [I32, I32]),
     "pgc_prefill_attn": (I32, [P, P, P, I64, P, I32, I32, F32, P, P, SZ, P]),
     "pgc_copy_rows": (I32, [P, P, P, P, I64, I64, I64, I64, P]),
     "pgc_kv_restore_dense": (I32, [P, P, I64, I64, P, P, I64, P, I64, I64, I64, P]),
@@ -189,8 +189,8 @@ def append_kv_rope(q_in, q_out, k_in, v_in, rope, positions, slots, k_pages, v_p
         "pgc_append_kv_rope")
 
 
-def prefill_workspace_bytes(chunk_len: int) -> int:
-    return int(lib().pgc_prefill_workspace_bytes(chunk_len))
+def prefill_workspace_bytes(prefix_len: int, chunk_len: int) -> int:
+    return int(lib().pgc_prefill_workspace_bytes(prefix_len, chunk_len))
 
 
 def prefill_attn(q, k_pages, v_pages, block_table, prefix_len, chunk_len, scale, out, workspace,

@@ -329,9 +329,9 @@ int pgc_merge_partials(const float *partials, int64_t rows, int num_parts, int64
                                              static_cast<cudaStream_t>(stream)));
 }
 
-size_t pgc_prefill_workspace_bytes(int chunk_len) {
-    if (chunk_len <= 0) return 0;
-    return prefill_workspace_bytes(chunk_len);
+size_t pgc_prefill_workspace_bytes(int prefix_len, int chunk_len) {
+    if (chunk_len <= 0 || prefix_len < 0) return 0;
+    return prefill_workspace_bytes(prefix_len, chunk_len, current_sm_count());
 }
 
 int pgc_prefill_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
@@ -346,12 +346,15 @@ int pgc_prefill_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t 
     if (chunk_len == 0) return PGC_OK;
     if (num_pages * 4 * 16 > INT32_MAX) return PGC_ERR_BOUNDS;
     if (!al16(q) || !al16(out) || !al16(k_pages) || !al16(v_pages)) return PGC_ERR_ALIGN;
-    if (workspace_bytes < prefill_workspace_bytes(chunk_len)) return PGC_ERR_WORKSPACE;
+    const size_t need = prefill_workspace_bytes(prefix_len, chunk_len, current_sm_count());
+    if (workspace_bytes < need || (need > 0 && !workspace)) return PGC_ERR_WORKSPACE;
+    if (((uintptr_t)workspace & 15u) != 0) return PGC_ERR_ALIGN;
     CUtensorMap tk, tv;
     if ((st = pool_tensor_map(k_pages, num_pages, &tk)) != PGC_OK) return st;
     if ((st = pool_tensor_map(v_pages, num_pages, &tv)) != PGC_OK) return st;
     return cuda_status(launch_prefill(q, tk, tv, num_pages, block_table, prefix_len, chunk_len,
-                                      scale, out, workspace, static_cast<cudaStream_t>(stream)));
+                                      scale, out, workspace, current_sm_count(),
+                                      static_cast<cudaStream_t>(stream)));
 }
 
 int pgc_copy_rows(void *dst, const void *src, const int32_t *dst_rows, const int32_t *src_rows,

@@ -41,6 +41,7 @@ enum ErrCode : int {
     kErrPosOutOfRange = 3,
     kErrWaitTimeout = 4,
     kErrTableOutOfRange = 5,
+    kErrSmemAlign = 6,
 };
 
 #define PGC_DEFINE_ERROR_WORD(name) static __device__ pgc::DevError name
@@ -138,6 +139,18 @@ __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
     return pol;
 }
 

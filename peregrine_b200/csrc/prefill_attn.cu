@@ -59,9 +59,11 @@ constexpr int kSmemBytesP = SmemP::kBytes + 1024;
 struct PrefillParams {
     const int32_t *block_table;
     uint16_t *out;
+    float *ws;  // nsplit > 1: partials [nsplit][chunk_len * 16][258] (m natural log, l, o)
     int64_t num_pages;
     int prefix_len;
     int chunk_len;
+    int nsplit;
     float scale_log2;
 };
 
@@ -189,6 +191,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const int n_keys = P + t_last + 1;  // keys any row of this tile may see
     const int n_tiles = (n_keys + kBN - 1) / kBN;
     const int total_keys = P + T;       // keys present in the cache
+    // this CTA's share of the key tiles (split z of nsplit; the host keeps every share >= 1)
+    const int tb = (int)((int64_t)n_tiles * blockIdx.z / p.nsplit);
+    const int n_loc = (int)((int64_t)n_tiles * (blockIdx.z + 1) / p.nsplit) - tb;
 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SmemP::kBar);
     uint64_t *q_full = bars + 0;
@@ -238,7 +243,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             const bool is_k = warp == 5;
             const CUtensorMap *tm = is_k ? &tmk : &tmv;
             tma_prefetch_desc(tm);
-            const uint64_t pol = l2_policy_evict_first();
+            // every q-tile CTA of a kv head streams the same K/V: ask L2 to keep it
+            const uint64_t pol = l2_policy_evict_last();
             if (is_k) {
                 tma_prefetch_desc(&tmq);
                 mbar_arrive_expect_tx(q_full, kQBytes);
@@ -248,10 +254,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             uint64_t *full = is_k ? k_full : v_full;
             uint64_t *empty = is_k ? k_empty : v_empty;
             uint8_t *ring = smem + (is_k ? SmemP::kK : SmemP::kV);
-            for (int j = 0; j < n_tiles; ++j) {
+            for (int j = 0; j < n_loc; ++j) {
                 const int b = j & 1;
                 if (j >= 2 && !wait_or_abort(&empty[b], ((j >> 1) - 1) & 1, abort_flag, 1)) break;
-                const int key0 = j * kBN;
+                const int key0 = (tb + j) * kBN;
                 int npg = 0;
                 for (int pp = 0; pp < kBN / kPage; ++pp)
                     if (key0 + pp * kPage < total_keys) ++npg;
@@ -295,8 +301,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             };
             bool ok = wait_or_abort(q_full, 0, abort_flag, 2);
             if (ok) ok = issue_s(0);
-            if (ok && n_tiles > 1) ok = issue_s(1);
-            for (int j = 0; ok && j < n_tiles; ++j) {
+            if (ok && n_loc > 1) ok = issue_s(1);
+            for (int j = 0; ok && j < n_loc; ++j) {
                 const int b = j & 1;
                 if (!wait_or_abort(&p_full[b], (j >> 1) & 1, abort_flag, 4) ||
                     !wait_or_abort(&v_full[b], (j >> 1) & 1, abort_flag, 5)) {
@@ -313,7 +319,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                              (j > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&v_empty[b]);
                 umma_commit(&p_free[b]);
-                if (j + 2 < n_tiles) ok = issue_s(j + 2);
+                if (j + 2 < n_loc) ok = issue_s(j + 2);
             }
         }
     } else {
@@ -326,7 +332,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int j = 0; j < n_tiles; ++j) {
+        for (int j = 0; j < n_loc; ++j) {
             const int b = j & 1;
             if (!wait_or_abort(&s_full[b], (j >> 1) & 1, abort_flag, 6)) { ok = false; break; }
             tc_fence_after();
@@ -339,7 +345,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 #pragma unroll
                 for (int i = 0; i < 32; ++i) { sv[i] = a[i]; sv[32 + i] = c2[i]; }
             }
-            const int key0 = j * kBN;
+            const int key0 = (tb + j) * kBN;
             float mx = -INFINITY;
             if (key0 + kBN - 1 <= vis && row_ok) {  // tile entirely visible: no per-key test
 #pragma unroll
@@ -419,17 +425,30 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             tc_fence_before();
             mbar_arrive(&p_full[b]);
         }
-        const int jl = n_tiles - 1;
+        const int jl = n_loc - 1;
         if (ok && wait_or_abort(&p_free[jl & 1], (jl >> 1) & 1, abort_flag, 9)) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            uint16_t *dst = p.out + ((int64_t)t * kNumQHeads + kvh * kGroup + g) * kHeadDim;
+            const int64_t orow = (int64_t)t * kNumQHeads + kvh * kGroup + g;
+            uint16_t *dst = p.out + orow * kHeadDim;
+            float *part = p.nsplit > 1
+                              ? p.ws + ((int64_t)blockIdx.z * T * kNumQHeads + orow) * kPartial
+                              : nullptr;
+            if (part != nullptr && row_ok) {
+                part[0] = (m == -INFINITY) ? -INFINITY : m * kLn2;  // natural-log units
+                part[1] = l;
+            }
 #pragma unroll 1
             for (int cc = 0; cc < kHeadDim / 32; ++cc) {
                 float o[32];
                 tmem_ld32(tmem + lane_addr + kTmemO + cc * 32, o);
                 tmem_wait_ld();
-                if (row_ok) {
+                if (!row_ok) continue;
+                if (part != nullptr) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2)
+                        *reinterpret_cast<float2 *>(part + 2 + cc * 32 + i) = make_float2(o[i], o[i + 1]);
+                } else {
 #pragma unroll
                     for (int i = 0; i < 32; i += 8) {
                         uint4 v;
@@ -455,16 +474,30 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 
 }  // namespace
 
-size_t prefill_workspace_bytes(int chunk_len) {
-    (void)chunk_len;
-    return 0;
+// Key-range splits per CTA. The kernel's K/V fetch path, not SM occupancy, limits it once
+// the grid covers every SM (one CTA per SM: 225 KiB of shared memory each), so the key range
+// is split only when the grid has fewer CTAs than SMs: then nsplit ~ SMs / CTAs (at most 8,
+// and never more shares than the smallest CTA has key tiles); the shares are merged by
+// merge_kernel.
+int prefill_nsplit(int prefix_len, int chunk_len, int sm_count) {
+    const int ctas = ((chunk_len + kTokTile - 1) / kTokTile) * kNumKvHeads;
+    const int min_tiles = (prefix_len + (chunk_len < kTokTile ? chunk_len : kTokTile) + kBN - 1) / kBN;
+    int ns = sm_count / ctas;
+    if (ns > 8) ns = 8;
+    if (ns > min_tiles) ns = min_tiles;
+    return ns < 1 ? 1 : ns;
+}
+
+size_t prefill_workspace_bytes(int prefix_len, int chunk_len, int sm_count) {
+    const int ns = prefill_nsplit(prefix_len, chunk_len, sm_count);
+    if (ns <= 1) return 0;
+    return (size_t)ns * chunk_len * kNumQHeads * kPartial * sizeof(float);
 }
 
 cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
                            int64_t num_pages, const int32_t *block_table, int prefix_len,
                            int chunk_len, float scale, uint16_t *out, void *workspace,
-                           cudaStream_t stream) {
-    (void)workspace;
+                           int sm_count, cudaStream_t stream) {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -476,16 +509,22 @@ cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUten
     }
     CUtensorMap tq;
     if (q_tensor_map(q, chunk_len, &tq) != PGC_OK) return cudaErrorInvalidValue;
+    const int ns = prefill_nsplit(prefix_len, chunk_len, sm_count);
     PrefillParams pp;
     pp.block_table = block_table;
     pp.out = out;
+    pp.ws = static_cast<float *>(workspace);
     pp.num_pages = num_pages;
     pp.prefix_len = prefix_len;
     pp.chunk_len = chunk_len;
+    pp.nsplit = ns;
     pp.scale_log2 = scale * kLog2e;
-    dim3 grid((chunk_len + kTokTile - 1) / kTokTile, kNumKvHeads);
+    dim3 grid((chunk_len + kTokTile - 1) / kTokTile, kNumKvHeads, ns);
     prefill_kernel<<<grid, kThreadsP, kSmemBytesP, stream>>>(tq, tk, tv, pp);
-    return cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || ns == 1) return e;
+    const int64_t rows = (int64_t)chunk_len * kNumQHeads;
+    return launch_merge_partials(pp.ws, rows, ns, rows * kPartial, nullptr, out, stream);
 }
 
 cudaError_t prefill_read_error(DevErrorHost *e, bool clear) {

@@ -25,13 +25,15 @@ def _setup(oracle, P, T, seed, spare=5, nan_tail=False):
 def _gpu(cuda, q, kp, vp, table, P, T):
     import torch
     out = torch.full((T, NQ, D), -1, dtype=torch.int16, device="cuda")
-    cuda.prefill_attn(dev(q), dev(kp), dev(vp), dev(table), P, T, SCALE, out, None)
+    nbytes = cuda.prefill_workspace_bytes(P, T)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device="cuda") if nbytes else None
+    cuda.prefill_attn(dev(q), dev(kp), dev(vp), dev(table), P, T, SCALE, out, ws)
     torch.cuda.synchronize()
     return host_u16(out)
 
 
 @pytest.mark.parametrize("P,T", [(0, 1), (0, 40), (100, 70), (1000, 33), (777, 129), (64, 64),
-                                 (5, 300)])
+                                 (5, 300), (3000, 37), (9000, 96)])
 def test_prefill_small(cuda, oracle, P, T):
     q, kp, vp, table = _setup(oracle, P, T, seed=P + T, nan_tail=True)
     got = _gpu(cuda, q, kp, vp, table, P, T)
@@ -61,3 +63,18 @@ def test_prefill_config2_shape(cuda, oracle):
     assert_attn_close(got[-1], dec)
     code, _ = cuda.device_error()
     assert code == 0
+
+
+def test_prefill_workspace_rules(cuda):
+    import torch
+    from peregrine_b200.capi import PgcError
+    assert cuda.prefill_workspace_bytes(24576, 1600) == 0  # config 2's grid covers the SMs
+    P, T = 24576, 96  # 12 CTAs: the key range is split, partials need a workspace
+    nbytes = cuda.prefill_workspace_bytes(P, T)
+    assert nbytes > 0 and nbytes % (T * NQ * 258 * 4) == 0
+    q = torch.zeros((T, NQ, D), dtype=torch.int16, device="cuda")
+    pool = torch.zeros(((P + T) // PAGE + 1, NKV, PAGE, D), dtype=torch.int16, device="cuda")
+    table = torch.arange(pool.shape[0], dtype=torch.int32, device="cuda")
+    small = torch.empty(16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(PgcError, match="WORKSPACE"):
+        cuda.prefill_attn(q, pool, pool, table, P, T, SCALE, q, small)
