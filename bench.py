@@ -445,6 +445,73 @@ def bench_config3(capi, iters=10):
             "GB_s": round(moved / (ms * 1e-3) / 1e9, 1)}
 
 
+def bench_config5b(capi, rank, world, iters=20, warmup=3):
+    """Config 5b: one 262144-token sequence (8 layers, 16q/4kv, d=256), context-parallel across
+    the ranks in contiguous page-aligned KV shards; per layer: q/k RoPE (the new K/V row lands
+    on the rank owning position 262144), split-K decode partials over the local shard, NCCL
+    all-gather of the (m, l, o) partials, LSE merge + gate on every rank."""
+    import torch
+    import torch.distributed as dist
+    from peregrine_b200 import cp
+    bf = torch.bfloat16
+    L, layers = 262144, LAYERS
+    cap = L + 1
+    s0, e0 = cp.shard_bounds(cap, world, rank)
+    n = e0 - s0
+    tail = cp.owner_of(L, cap, world)
+    pages = max(1, (n + PAGE - 1) // PAGE)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5000 + rank)
+    kp = [torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+    vp = [torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+    table = torch.arange(pages, dtype=torch.int32, device="cuda").view(1, -1)
+    local_len = torch.tensor([n], dtype=torch.int32, device="cuda")
+    gq = torch.Generator(device="cuda")
+    gq.manual_seed(77)  # the query side is identical on every rank
+    q_in = [torch.randn((1, NQ, 2 * D), dtype=bf, device="cuda", generator=gq) for _ in range(layers)]
+    k_in = [torch.randn((1, NKV, D), dtype=bf, device="cuda", generator=gq) for _ in range(layers)]
+    v_in = [torch.randn((1, NKV, D), dtype=bf, device="cuda", generator=gq) for _ in range(layers)]
+    q = torch.empty((1, NQ, D), dtype=bf, device="cuda")
+    gate = torch.empty((1, NQ, D), dtype=bf, device="cuda")
+    out = torch.empty((NQ, D), dtype=bf, device="cuda")
+    partial = torch.empty((NQ, 258), dtype=torch.float32, device="cuda")
+    gathered = torch.empty((world, NQ, 258), dtype=torch.float32, device="cuda")
+    ws = torch.empty(capi.decode_workspace_bytes(1, 1, max(n, 1)), dtype=torch.uint8, device="cuda")
+    rope = torch.from_numpy(capi.rope_table(cap)).cuda()
+    pos = torch.tensor([L], dtype=torch.int32, device="cuda")
+    slot_val = (L - s0) if rank == tail else -1
+    slot = torch.tensor([slot_val], dtype=torch.int64, device="cuda")
+    s = torch.cuda.current_stream()
+
+    def step():
+        for l in range(layers):
+            capi.append_kv_rope(q_in[l], q, k_in[l], v_in[l], rope, pos, slot, kp[l], vp[l],
+                                gate_out=gate, stream=s)
+            cp.cp_decode_layer(q.view(1, 1, NQ, D), kp[l], vp[l], table, local_len, n, SCALE,
+                               partial, gathered, ws, out, gate=gate.view(NQ, D), stream=s)
+
+    for _ in range(warmup):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for _ in range(iters):
+        step()
+    b.record(s)
+    torch.cuda.synchronize()
+    ms = torch.tensor([a.elapsed_time(b) / iters], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    kv = layers * cap * KV_BYTES_PER_TOKEN
+    return {"workload": f"config5b: one 262144-token sequence, 8 layers, context-parallel over "
+                        f"{world} GPU(s) ({n} tokens on rank {rank}), NCCL all-gather of partials",
+            "ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1),
+            "GB_s_aggregate": round(kv / (ms * 1e-3) / 1e9, 1), "kv_bytes": kv}
+
+
 # ------------------------------------------------------------------------------ GPU arm
 
 def run_ours(args, rank, world, local_rank):
@@ -566,6 +633,12 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(tb)
     all_bytes, all_kv, all_seqs = (float(x) for x in tb.tolist())
+    cfg5b = None
+    if args.workload == "config4" and not args.no_configs:
+        kpool.clear()
+        vpool.clear()
+        torch.cuda.empty_cache()
+        cfg5b = bench_config5b(capi, rank, world)
     if rank != 0:
         return
     step_ms = ms / args.steps
@@ -599,12 +672,11 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": args.steps * layers * 3,
         "clocks": clk,
     }
-    if world == 1 and args.workload == "config4" and not args.no_configs:
-        kpool.clear()
-        vpool.clear()
-        torch.cuda.empty_cache()
-        line["configs"] = {"config1": bench_config1(capi), "config2": bench_config2(capi),
-                           "config3": bench_config3(capi)}
+    if cfg5b is not None:
+        line["configs"] = {"config5b": cfg5b}
+        if world == 1:
+            line["configs"].update({"config1": bench_config1(capi), "config2": bench_config2(capi),
+                                    "config3": bench_config3(capi)})
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         gbs, dt, desc = cpu_sample(lens, threads, max_tokens=1 << 30, min_seconds=10.0)
@@ -632,7 +704,8 @@ def main():
         from peregrine_b200 import capi
         torch.cuda.set_device(local_rank)
         print(json.dumps({"configs": {"config1": bench_config1(capi), "config2": bench_config2(capi),
-                                      "config3": bench_config3(capi)}}), flush=True)
+                                      "config3": bench_config3(capi),
+                                      "config5b": bench_config5b(capi, 0, 1)}}), flush=True)
         return
     try:
         run_ours(args, rank, world, local_rank)
