@@ -39,8 +39,12 @@ def owner_of(position: int, total_capacity: int, world: int) -> int:
 
 
 def gather_partials(local, gathered, group=None) -> None:
-    """All-gather the local partials [rows, 258] into gathered [world, rows, 258]."""
+    """All-gather the local partials [rows, 258] into gathered [world, rows, 258]. A single
+    rank (no process group) simply copies its own partials."""
     import torch.distributed as dist
+    if not dist.is_initialized() or gathered.shape[0] == 1:
+        gathered[0].copy_(local)
+        return
     if dist.get_backend(group) == "nccl":
         dist.all_gather_into_tensor(gathered, local, group=group)
     else:

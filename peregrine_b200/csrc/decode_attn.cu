@@ -32,6 +32,11 @@ namespace {
 constexpr int kConsumers = 4;
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kStages = 4;
+// Page i goes to stage i % kStages and to consumer warp i % kConsumers. The stage count must be
+// a multiple of the consumer count so that every stage has exactly one consumer, which waits
+// on it phase after phase; with a stage shared by two warps, a warp running ahead would wait
+// on the parity of a phase two steps ahead, which an mbarrier reports as already complete.
+static_assert(kStages % kConsumers == 0, "each stage must belong to one consumer warp");
 constexpr int kTileBytes = kPage * kHeadDim * 2;  // one (page, kv head) of K or V: 8 KiB
 constexpr int kStageBytes = 2 * kTileBytes;
 constexpr int kQRowBytes = kHeadDim * 2 + 16;  // padded row: conflict-free ldmatrix
@@ -53,7 +58,7 @@ struct SplitParams {
 
 struct SmemLayout {
     static constexpr int kStageOff = 0;                            // 1024-aligned
-    static constexpr int kQOff = kStageOff + kStages * kStageBytes;  // 65536
+    static constexpr int kQOff = kStageOff + kStages * kStageBytes;
     static constexpr int kMOff = kQOff + 16 * kQRowBytes;
     static constexpr int kLOff = kMOff + kConsumers * 16 * 4;
     static constexpr int kBarOff = kLOff + kConsumers * 16 * 4;
@@ -411,7 +416,9 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
 DecodePlan decode_plan(int batch, int max_seq_len, int sm_count) {
     const int64_t max_pages = (max_seq_len + kPage - 1) / kPage;
     const int64_t units = (int64_t)batch * kNumKvHeads * max_pages;
-    const int64_t target_ctas = (int64_t)sm_count * 2 * 4;
+    // One wave of resident CTAs (2 per SM): fewer, longer splits amortise each CTA's prologue
+    // and epilogue; long batches hit the 64-page cap anyway.
+    const int64_t target_ctas = (int64_t)sm_count * 2;
     int64_t pps = (units + target_ctas - 1) / target_ctas;
     if (pps < kMinPagesPerSplit) pps = kMinPagesPerSplit;
     if (pps > kMaxPagesPerSplit) pps = kMaxPagesPerSplit;
