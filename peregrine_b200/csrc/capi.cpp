@@ -352,7 +352,7 @@ int pgc_prefill_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t 
     CUtensorMap tk, tv;
     if ((st = pool_tensor_map(k_pages, num_pages, &tk)) != PGC_OK) return st;
     if ((st = pool_tensor_map(v_pages, num_pages, &tv)) != PGC_OK) return st;
-    return cuda_status(launch_prefill(q, tk, tv, num_pages, block_table, prefix_len, chunk_len,
+    return cuda_status(launch_prefill(q, tk, tv, v_pages, num_pages, block_table, prefix_len, chunk_len,
                                       scale, out, workspace, current_sm_count(),
                                       static_cast<cudaStream_t>(stream)));
 }

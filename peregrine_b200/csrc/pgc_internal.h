@@ -75,7 +75,7 @@ cudaError_t copy_read_error(DevErrorHost *e, bool clear);
 int prefill_nsplit(int prefix_len, int chunk_len, int sm_count);
 size_t prefill_workspace_bytes(int prefix_len, int chunk_len, int sm_count);
 cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
-                           int64_t num_pages, const int32_t *block_table, int prefix_len,
+                           const uint16_t *v_pages, int64_t num_pages, const int32_t *block_table, int prefix_len,
                            int chunk_len, float scale, uint16_t *out, void *workspace,
                            int sm_count, cudaStream_t stream);
 cudaError_t prefill_read_error(DevErrorHost *e, bool clear);

@@ -28,6 +28,29 @@ namespace pgc {
 
 PGC_DEFINE_ERROR_WORD(g_prefill_err);
 
+#ifdef PGC_PREFILL_TRACE
+// Diagnostic build only: per-CTA progress of the pair kernel (rank, MMA and softmax steps).
+static __device__ int g_pair_diag[256][8];
+#define PF_DIAG(field, val)                                                                   \
+    do {                                                                                      \
+        const int cid_ = blockIdx.x + blockIdx.y * gridDim.x;                                 \
+        if (cid_ < 256) g_pair_diag[cid_][field] = (val);                                     \
+    } while (0)
+static __device__ long long g_pair_trace[8][512];
+#define PF_TRACE(ev, j)                                                                       \
+    do {                                                                                      \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) < 512)              \
+            g_pair_trace[ev][j] = clock64();                                                  \
+    } while (0)
+#else
+#define PF_TRACE(ev, j) \
+    do {                \
+    } while (0)
+#define PF_DIAG(field, val) \
+    do {                    \
+    } while (0)
+#endif
+
 namespace {
 
 constexpr int kBM = 128;           // rows = 32 tokens x 4 heads
@@ -58,6 +81,7 @@ constexpr int kSmemBytesP = SmemP::kBytes + 1024;
 
 struct PrefillParams {
     const int32_t *block_table;
+    const uint16_t *v_pages;  // V pool (the pair kernel copies a partial final page directly)
     uint16_t *out;
     float *ws;  // nsplit > 1: partials [nsplit][chunk_len * 16][258] (m natural log, l, o)
     int64_t num_pages;
@@ -168,7 +192,9 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
             if (*abort_flag) return false;
             if (global_timer_ns() - t0 > 2000000000ull || i > (1u << 30)) {
                 record_error(&g_prefill_err, kErrWaitTimeout, where);
+#ifndef PGC_PREFILL_NO_ABORT
                 *abort_flag = 1;
+#endif
                 return false;
             }
         }
@@ -472,6 +498,546 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
 }
 
+
+// ---------------------------------------------------------------- two-SM (cta_group::2) helpers
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+          "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]),
+          "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    // non-.aligned forms: producer and MMA warps arrive with diverged lanes
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Arrive (with transaction bytes) on an mbarrier that may live in another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t bar_cluster, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;"
+                 ::"r"(bar_cluster), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
+
+// Waits with acquire at cluster scope (the barrier is signalled from the peer CTA too).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// 2-D tiled TMA load into this CTA's shared memory whose completion bytes are counted on the
+// pair leader's mbarrier (`bar_leader`: a shared::cluster address in CTA 0).
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tmap, int32_t x,
+                                                 int32_t y, uint32_t bar_leader, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar_leader), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void *smem_dst, const void *tmap, int32_t x,
+                                                 int32_t y, int32_t z, uint32_t bar_leader) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar_leader)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma2_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma2_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                         uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Completion of this thread's earlier pair MMAs arrives once on the mbarrier at this shared
+// offset in BOTH CTAs of the pair (commit arrive with CTA mask 0b11; an mbarrier signal, not a
+// data load).
+__device__ __forceinline__ void umma2_commit_pair(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+        ::"r"(smem_u32(bar)), "h"((uint16_t)3)
+        : "memory");
+}
+
+// Bounded wait with cluster-scope acquire, for barriers that the peer CTA arrives on.
+__device__ __forceinline__ bool wait_or_abort_cluster(uint64_t *bar, uint32_t parity,
+                                                      volatile int *abort_flag, int where) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (global_timer_ns() - t0 > 2000000000ull || i > (1u << 30)) {
+                record_error(&g_prefill_err, kErrWaitTimeout, where);
+#ifndef PGC_PREFILL_NO_ABORT
+                *abort_flag = 1;
+#endif
+                return false;
+            }
+        }
+    }
+}
+
+// =============================================================================================
+// Two-SM prefill (tcgen05 cta_group::2). A cluster of two CTAs runs one kv head for two adjacent
+// 32-token query tiles: M = 256 rows (each CTA's 128 rows = its 32 tokens x 4 heads). Every
+// MMA is issued by the pair leader (cluster rank 0) and reads each CTA's half of both operands
+// from that CTA's shared memory or TMEM: for S = Q K^T (M256 N128) each CTA stages its own Q and
+// 64 of the tile's 128 keys; for O += P V (M256 N256) each CTA holds its P rows in TMEM and 128
+// of the 256 value dims. Each SM therefore fetches half of every K/V tile that a one-SM CTA
+// would, for the same tensor work.
+// =============================================================================================
+namespace pair {
+
+constexpr int kThreads = 352;         // warps 0-7 softmax, 8 MMA, 9 K (+Q) TMA, 10 V TMA
+constexpr int kBNp = 128;             // keys per tile
+constexpr int kQBytesP = kBM * kHeadDim * 2;      // [4 dim blocks][128 rows][128 B] = 64 KiB
+constexpr int kKHalf = 64 * kHeadDim * 2;         // this CTA's 64 keys: [4][64][128 B] = 32 KiB
+constexpr int kVHalf = kBNp * 128 * 2;            // this CTA's 128 dims: [2][128][128 B] = 32 KiB
+constexpr int kKSlotsP = 3;
+constexpr int kVSlotsP = 2;
+constexpr uint32_t kTO = 0;           // O: 256 columns
+constexpr uint32_t kTS = 256;         // S tiles: 2 x 128 columns; P(j) over the first 64 of S(j)
+
+struct Smem2 {
+    static constexpr int kQ = 0;
+    static constexpr int kK = kQ + kQBytesP;
+    static constexpr int kV = kK + kKSlotsP * kKHalf;
+    static constexpr int kBar = kV + kVSlotsP * kVHalf;
+    // leader-side: q_full, k_full[3], v_full[2], p_full[2]; both sides: k_empty[3],
+    // v_empty[2], s_full[2], pv_done[2]
+    static constexpr int kNumBars = 1 + kKSlotsP + kVSlotsP + 2 + kKSlotsP + kVSlotsP + 2 + 2;
+    static constexpr int kRed = kBar + kNumBars * 8;
+    static constexpr int kTmemSlot = kRed + 2 * 2 * kBM * 4;
+    static constexpr int kAbort = kTmemSlot + 8;
+    static constexpr int kBytes = kTmemSlot + 16;
+};
+static_assert(Smem2::kBytes <= 232448, "pair prefill shared memory exceeds the sm_100 limit");
+
+}  // namespace pair
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
+    prefill_pair_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, const PrefillParams p) {
+    using namespace pair;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    // The two CTAs of a pair must agree on the layout; a misaligned window would break it, and
+    // both CTAs see the same alignment, so both leave together.
+    if ((smem_u32(smem) & 1023u) != 0) {
+        if (threadIdx.x == 0) record_error(&g_prefill_err, kErrSmemAlign, 0);
+        return;
+    }
+
+    const int qt = blockIdx.x;  // this CTA's 32-token tile; the pair is (2c, 2c+1)
+    const int kvh = blockIdx.y;
+    const int T = p.chunk_len, P = p.prefix_len;
+    const int tok0 = qt * kTokTile;
+    const int pair_last = min(((qt >> 1) << 1) * kTokTile + 2 * kTokTile - 1, T - 1);
+    const int n_keys = P + pair_last + 1;  // keys any row of the pair may see
+    const int n_tiles = (n_keys + kBNp - 1) / kBNp;
+    const int total_keys = P + T;
+    const int tb = (int)((int64_t)n_tiles * blockIdx.z / p.nsplit);
+    const int n_loc = (int)((int64_t)n_tiles * (blockIdx.z + 1) / p.nsplit) - tb;
+
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Smem2::kBar);
+    uint64_t *q_full = bars;                       // leader: both CTAs' Q bytes
+    uint64_t *k_full = q_full + 1;                 // leader [3]: both CTAs' K halves
+    uint64_t *v_full = k_full + kKSlotsP;          // leader [2]: both CTAs' V halves
+    uint64_t *p_full = v_full + kVSlotsP;          // leader [2]: 16 softmax-warp arrivals
+    uint64_t *k_empty = p_full + 2;                // each [3]
+    uint64_t *v_empty = k_empty + kKSlotsP;        // each [2]
+    uint64_t *s_full = v_empty + kVSlotsP;         // each [2]
+    uint64_t *pv_done = s_full + 2;                // each [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Smem2::kTmemSlot);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + Smem2::kAbort);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        mbar_init(q_full, 2);
+        for (int s = 0; s < kKSlotsP; ++s) {
+            mbar_init(&k_full[s], 2);
+            mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < kVSlotsP; ++s) {
+            mbar_init(&v_full[s], 2);  // leader: both CTAs' V halves
+            mbar_init(&v_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&p_full[b], 16);
+            mbar_init(&s_full[b], 1);
+            mbar_init(&pv_done[b], 1);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync_all();  // both CTAs' barriers are initialised before anyone signals them
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) PF_DIAG(0, 100 + (int)rank);
+    auto leader_addr = [&](uint64_t *bar) { return cluster_map(smem_u32(bar), 0); };
+
+    if (warp == 9) {
+        // ------------------------------------------------------------ TMA: Q and this CTA's K half
+        if (lane == 0) {
+            tma_prefetch_desc(&tmq);
+            tma_prefetch_desc(&tmk);
+            const uint64_t pol = l2_policy_evict_last();
+            const uint32_t qbar = leader_addr(q_full);
+            mbar_arrive_expect_tx_cluster(qbar, kQBytesP);
+            for (int c = 0; c < 4; ++c)
+                tma_load_3d_pair(smem + Smem2::kQ + c * (kBM * 128), &tmq, c * 64, kvh * kGroup, tok0, qbar);
+            for (int j = 0; j < n_loc; ++j) {
+                const int sl = j % kKSlotsP;
+                if (j >= kKSlotsP &&
+                    !wait_or_abort(&k_empty[sl], ((j / kKSlotsP) - 1) & 1, abort_flag, 1))
+                    break;
+                const int key0 = (tb + j) * kBNp + (int)rank * 64;  // this CTA's 64 keys
+                int npg = 0;
+                for (int pp = 0; pp < 4; ++pp)
+                    if (key0 + pp * kPage < total_keys) ++npg;
+                const uint32_t kbar = leader_addr(&k_full[sl]);
+                mbar_arrive_expect_tx_cluster(kbar, (uint32_t)npg * 4 * 2048);
+                uint8_t *dst = smem + Smem2::kK + sl * kKHalf;
+                for (int pp = 0; pp < npg; ++pp) {
+                    int page = p.block_table[(key0 >> 4) + pp];
+                    if (page < 0 || page >= p.num_pages) {
+                        record_error(&g_prefill_err, kErrPageOutOfRange, page);
+                        page = 0;
+                    }
+                    const int row = (page * kNumKvHeads + kvh) * kPage;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        tma_load_2d_pair(dst + c * (64 * 128) + pp * 2048, &tmk, c * 64, row, kbar, pol);
+                }
+            }
+        }
+    } else if (warp == 10) {
+        // ------------------------------------------------------------ TMA: this CTA's V half
+        // (value dims [128 * rank, +128) of all 128 keys), counted on the leader's barrier like
+        // K. Rows past the cache end are zeroed here and a partial final page is copied row by
+        // row by the whole warp, so no stale slot (possibly a NaN pattern) meets a zero
+        // probability in P.V, and the softmax warps never wait on V.
+        {
+            if (lane == 0) tma_prefetch_desc(&tmv);
+            const uint64_t pol = l2_policy_evict_last();
+            for (int j = 0; j < n_loc; ++j) {
+                const int sl = j % kVSlotsP;
+                bool go = true;
+                if (lane == 0 && j >= kVSlotsP)
+                    go = wait_or_abort(&v_empty[sl], ((j / kVSlotsP) - 1) & 1, abort_flag, 11);
+                if (!__shfl_sync(0xffffffffu, go ? 1 : 0, 0)) break;
+                const int key0 = (tb + j) * kBNp;
+                const int valid = min(kBNp, total_keys - key0);  // keys of this tile in the cache
+                const int full_pages = valid / kPage;            // loaded by TMA
+                uint8_t *dst = smem + Smem2::kV + sl * kVHalf;
+                if (valid < kBNp) {
+                    // rows [full_pages*16, 128): zero, then copy the partial page's valid rows
+                    const int first = full_pages * kPage;
+                    for (int i = lane; i < (kBNp - first) * 2 * 8; i += 32) {
+                        const int row = first + i / 16;
+                        const int u = i % 16;
+                        *reinterpret_cast<uint4 *>(dst + (u >> 3) * (kBNp * 128) + row * 128 + (u & 7) * 16) =
+                            make_uint4(0, 0, 0, 0);
+                    }
+                    __syncwarp();
+                    const int tail = valid - first;  // valid rows in the partial page (0..15)
+                    if (tail > 0) {
+                        int page = p.block_table[(key0 >> 4) + full_pages];
+                        if (page < 0 || page >= p.num_pages) {
+                            if (lane == 0) record_error(&g_prefill_err, kErrPageOutOfRange, page);
+                            page = 0;
+                        }
+                        const uint16_t *src = p.v_pages + ((int64_t)(page * kNumKvHeads + kvh) * kPage) * kHeadDim;
+                        for (int i = lane; i < tail * 2 * 8; i += 32) {
+                            const int rr = i / 16, u = i % 16;  // row in page, 16-B unit of 2 blocks
+                            const int db = u >> 3, unit = u & 7;
+                            const uint4 v = *reinterpret_cast<const uint4 *>(
+                                src + (int64_t)rr * kHeadDim + ((int)rank * 2 + db) * 64 + unit * 8);
+                            const int row = first + rr;
+                            *reinterpret_cast<uint4 *>(dst + db * (kBNp * 128) + row * 128 +
+                                                       ((unit ^ (row & 7)) << 4)) = v;
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                }
+                if (lane == 0) {
+                    const uint32_t vbar = leader_addr(&v_full[sl]);
+                    mbar_arrive_expect_tx_cluster(vbar, (uint32_t)full_pages * 2 * 2048);
+                    PF_DIAG(7, j + 1);
+                    for (int pp = 0; pp < full_pages; ++pp) {
+                        int page = p.block_table[(key0 >> 4) + pp];
+                        if (page < 0 || page >= p.num_pages) {
+                            record_error(&g_prefill_err, kErrPageOutOfRange, page);
+                            page = 0;
+                        }
+                        const int row = (page * kNumKvHeads + kvh) * kPage;
+#pragma unroll
+                        for (int db = 0; db < 2; ++db)
+                            tma_load_2d_pair(dst + db * (kBNp * 128) + pp * 2048, &tmv,
+                                             ((int)rank * 2 + db) * 64, row, vbar, pol);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == 8) {
+        // ------------------------------------------------------------ pair MMA issuer (leader)
+        if (leader && lane == 0) {
+            constexpr uint32_t idesc_s = umma_idesc(2 * kBM, kBNp, false, false);
+            constexpr uint32_t idesc_o = umma_idesc(2 * kBM, kHeadDim, false, true);
+            const uint32_t q_addr = smem_u32(smem + Smem2::kQ);
+            auto both = [&](uint64_t *bar) { umma2_commit_pair(bar); };
+            auto issue_s = [&](int jj) -> bool {
+                const int b = jj & 1;
+                const int sl = jj % kKSlotsP;
+                if (!wait_or_abort(&k_full[sl], (jj / kKSlotsP) & 1, abort_flag, 3)) return false;
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(smem + Smem2::kK + sl * kKHalf);
+#pragma unroll
+                for (int kk = 0; kk < kHeadDim / 16; ++kk)
+                    umma2_ss(tmem + kTS + b * kBNp,
+                             umma_desc(q_addr + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024),
+                             umma_desc(k_addr + (kk >> 2) * (64 * 128) + (kk & 3) * 32, 16, 1024),
+                             idesc_s, kk > 0 ? 1u : 0u);
+                both(&k_empty[sl]);
+                both(&s_full[b]);
+                return true;
+            };
+            bool ok = wait_or_abort(q_full, 0, abort_flag, 2);
+            if (ok) ok = issue_s(0);
+            if (ok && n_loc > 1) ok = issue_s(1);
+            PF_DIAG(2, ok ? 1 : -1);
+            for (int j = 0; ok && j < n_loc; ++j) {
+                const int b = j & 1;
+                const int sl = j % kVSlotsP;
+                if (!wait_or_abort_cluster(&p_full[b], (j >> 1) & 1, abort_flag, 4) ||
+                    !wait_or_abort_cluster(&v_full[sl], (j / kVSlotsP) & 1, abort_flag, 5)) {
+                    ok = false;
+                    break;
+                }
+                PF_DIAG(3, j + 1);
+                PF_TRACE(0, j);
+                tc_fence_after();
+                const uint32_t v_addr = smem_u32(smem + Smem2::kV + sl * kVHalf);
+#pragma unroll
+                for (int kk = 0; kk < kBNp / 16; ++kk)
+                    umma2_ts(tmem + kTO, tmem + kTS + b * kBNp + kk * 8,
+                             umma_desc(v_addr + kk * 2048, kBNp * 128, 1024), idesc_o,
+                             (j > 0 || kk > 0) ? 1u : 0u);
+                both(&v_empty[sl]);
+                both(&pv_done[b]);
+                PF_TRACE(1, j);
+                if (j + 2 < n_loc) ok = issue_s(j + 2);
+                PF_TRACE(2, j);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ softmax + epilogue
+        // Warps w and w+4 share TMEM lanes 32*(w%4)..+31 (one accumulator row per thread) and
+        // split each 128-key S tile into key halves [64*h, +64) and O into dims [128*h, +128).
+        const int qd = warp & 3;
+        const int h = warp >> 2;
+        const int r = qd * 32 + lane;
+        const int t = tok0 + r / kGroup;
+        const int g = r % kGroup;
+        const bool row_ok = t < T;
+        const int vis = P + t;
+        const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
+        const int64_t orow = (int64_t)t * kNumQHeads + kvh * kGroup + g;
+        float *red = reinterpret_cast<float *>(smem + Smem2::kRed);
+        const uint32_t pbar[2] = {leader_addr(&p_full[0]), leader_addr(&p_full[1])};
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_loc; ++j) {
+            const int b = j & 1;
+            if (!wait_or_abort(&s_full[b], (j >> 1) & 1, abort_flag, 6)) { ok = false; break; }
+            tc_fence_after();
+            float sv[64];
+            {
+                float a[32], c2[32];
+                if (threadIdx.x == 0) PF_DIAG(4, j + 1);
+                if (threadIdx.x == 0) PF_TRACE(3, j);
+                tmem_ld32(tmem + lane_addr + kTS + b * kBNp + h * 64, a);
+                tmem_ld32(tmem + lane_addr + kTS + b * kBNp + h * 64 + 32, c2);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) { sv[i] = a[i]; sv[32 + i] = c2[i]; }
+            }
+            const int tile0 = (tb + j) * kBNp;
+            const int key0 = tile0 + h * 64;
+            float mx = -INFINITY;
+            if (key0 + 63 <= vis && row_ok) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    sv[i] *= p.scale_log2;
+                    mx = fmaxf(mx, sv[i]);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    sv[i] = (row_ok && key0 + i <= vis) ? sv[i] * p.scale_log2 : -INFINITY;
+                    mx = fmaxf(mx, sv[i]);
+                }
+            }
+            red[(b * 2 + h) * kBM + r] = mx;
+            // both halves have read S tile b before either overwrites it with P
+            asm volatile("bar.sync %0, 64;" ::"r"(1 + qd) : "memory");
+            mx = fmaxf(mx, red[(b * 2 + (h ^ 1)) * kBM + r]);
+            const float m_new = fmaxf(m, mx);
+            float corr = 1.f;
+            if (m_new > m + kLazyRescale) {
+                corr = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
+                m = m_new;
+            }
+            const float m_use = (m == -INFINITY) ? 0.f : m;
+            float ps = 0.f;
+            uint32_t pw[32];
+#pragma unroll
+            for (int i = 0; i < 64; i += 2) {
+                const float a0 = fast_exp2(sv[i] - m_use);
+                const float a1 = fast_exp2(sv[i + 1] - m_use);
+                ps += a0 + a1;
+                pw[i >> 1] = pack_bf16x2(a0, a1);
+            }
+            l = l * corr + ps;
+            if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+                if (!wait_or_abort(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 7)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int cc = 0; cc < 4; ++cc) {
+                    float o[32];
+                    const uint32_t col = kTO + h * 128 + cc * 32;
+                    tmem_ld32(tmem + lane_addr + col, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= corr;
+                    tmem_st32(tmem + lane_addr + col, o);
+                }
+            }
+            {
+                uint32_t lo[16], hi[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) { lo[i] = pw[i]; hi[i] = pw[16 + i]; }
+                tmem_st16u(tmem + lane_addr + kTS + b * kBNp + h * 32, lo);
+                tmem_st16u(tmem + lane_addr + kTS + b * kBNp + h * 32 + 16, hi);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(pbar[b]);
+            if (threadIdx.x == 0) PF_DIAG(6, j + 1);
+            if (threadIdx.x == 0) PF_TRACE(4, j);
+        }
+        const int jl = n_loc - 1;
+        if (ok && wait_or_abort(&pv_done[jl & 1], (jl >> 1) & 1, abort_flag, 9)) {
+            tc_fence_after();
+            red[h * kBM + r] = l;
+            asm volatile("bar.sync %0, 64;" ::"r"(1 + qd) : "memory");
+            const float l_row = l + red[(h ^ 1) * kBM + r];
+            const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+            uint16_t *dst = p.out + orow * kHeadDim;
+            float *part = p.nsplit > 1
+                              ? p.ws + ((int64_t)blockIdx.z * T * kNumQHeads + orow) * kPartial
+                              : nullptr;
+            if (part != nullptr && row_ok && h == 0) {
+                part[0] = (m == -INFINITY) ? -INFINITY : m * kLn2;
+                part[1] = l_row;
+            }
+#pragma unroll 1
+            for (int cc = 0; cc < 4; ++cc) {
+                float o[32];
+                const int col = h * 128 + cc * 32;
+                tmem_ld32(tmem + lane_addr + kTO + col, o);
+                tmem_wait_ld();
+                if (!row_ok) continue;
+                if (part != nullptr) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2)
+                        *reinterpret_cast<float2 *>(part + 2 + col + i) = make_float2(o[i], o[i + 1]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        uint4 v;
+                        v.x = pack_bf16x2(o[i] * inv, o[i + 1] * inv);
+                        v.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+                        v.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+                        v.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+                        *reinterpret_cast<uint4 *>(dst + col + i) = v;
+                    }
+                }
+            }
+        }
+    }
+    // neither CTA may leave (or free TMEM) while the pair MMA or the peer can still touch it
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
 }  // namespace
 
 // Key-range splits per CTA. The kernel's K/V fetch path, not SM occupancy, limits it once
@@ -480,8 +1046,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 // and never more shares than the smallest CTA has key tiles); the shares are merged by
 // merge_kernel.
 int prefill_nsplit(int prefix_len, int chunk_len, int sm_count) {
-    const int ctas = ((chunk_len + kTokTile - 1) / kTokTile) * kNumKvHeads;
-    const int min_tiles = (prefix_len + (chunk_len < kTokTile ? chunk_len : kTokTile) + kBN - 1) / kBN;
+    const int qtiles = (chunk_len + kTokTile - 1) / kTokTile;
+    const int ctas = ((qtiles + 1) / 2) * 2 * kNumKvHeads;  // CTA pairs
+    const int min_tiles = (prefix_len + (chunk_len < kTokTile ? chunk_len : kTokTile) + 127) / 128;
     int ns = sm_count / ctas;
     if (ns > 8) ns = 8;
     if (ns > min_tiles) ns = min_tiles;
@@ -495,15 +1062,22 @@ size_t prefill_workspace_bytes(int prefix_len, int chunk_len, int sm_count) {
 }
 
 cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
-                           int64_t num_pages, const int32_t *block_table, int prefix_len,
+                           const uint16_t *v_pages, int64_t num_pages, const int32_t *block_table, int prefix_len,
                            int chunk_len, float scale, uint16_t *out, void *workspace,
                            int sm_count, cudaStream_t stream) {
+#ifdef PGC_PREFILL_ONE_SM
+    auto kern = prefill_kernel;
+    const int smem_bytes = kSmemBytesP, threads = kThreadsP, xmul = 1;
+#else
+    auto kern = prefill_pair_kernel;
+    const int smem_bytes = pair::Smem2::kBytes, threads = pair::kThreads, xmul = 2;
+#endif
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytesP);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smem_bytes);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -512,6 +1086,7 @@ cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUten
     const int ns = prefill_nsplit(prefix_len, chunk_len, sm_count);
     PrefillParams pp;
     pp.block_table = block_table;
+    pp.v_pages = v_pages;
     pp.out = out;
     pp.ws = static_cast<float *>(workspace);
     pp.num_pages = num_pages;
@@ -519,8 +1094,9 @@ cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUten
     pp.chunk_len = chunk_len;
     pp.nsplit = ns;
     pp.scale_log2 = scale * kLog2e;
-    dim3 grid((chunk_len + kTokTile - 1) / kTokTile, kNumKvHeads, ns);
-    prefill_kernel<<<grid, kThreadsP, kSmemBytesP, stream>>>(tq, tk, tv, pp);
+    const int qtiles = (chunk_len + kTokTile - 1) / kTokTile;
+    dim3 grid((qtiles + xmul - 1) / xmul * xmul, kNumKvHeads, ns);
+    kern<<<grid, threads, smem_bytes, stream>>>(tq, tk, tv, pp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || ns == 1) return e;
     const int64_t rows = (int64_t)chunk_len * kNumQHeads;
@@ -535,3 +1111,15 @@ cudaError_t prefill_read_error(DevErrorHost *e, bool clear) {
 }
 
 }  // namespace pgc
+
+#ifdef PGC_PREFILL_TRACE
+extern "C" int pgc_debug_pair_diag(int *out) {
+    return cudaMemcpyFromSymbol(out, pgc::g_pair_diag, sizeof(int) * 256 * 8) == cudaSuccess ? 0 : -4;
+}
+#endif
+
+#ifdef PGC_PREFILL_TRACE
+extern "C" int pgc_debug_pair_trace(long long *out) {
+    return cudaMemcpyFromSymbol(out, pgc::g_pair_trace, sizeof(long long) * 8 * 512) == cudaSuccess ? 0 : -4;
+}
+#endif
