@@ -9,16 +9,15 @@
 // materialises S and P in bf16 per kv head; here they never leave the SM: S lives in TMEM, P
 // in shared memory, and the softmax is online (fp32), so only Q, K, V and O touch HBM.
 //
-// CTA = one kv head x 32 query tokens. The 4 GQA heads of the kv head are stacked into the
-// MMA's M = 128 rows (row r = token r/4, head r%4), so every K/V tile is loaded once for 4
-// heads. Warp roles (224 threads):
-//   warps 0-3  softmax + epilogue, thread r owns accumulator row r (TMEM lane r);
-//   warp 4     MMA issuer (one lane): S = Q K^T (M128 N64 K256), O += P V (M128 N256);
-//   warp 5     TMA producer of Q and of the K tiles (64 keys = 4 pages) into a 2-slot ring;
-//   warp 6     TMA producer of the V tiles into their own 2-slot ring.
-// S and P are double-buffered (TMEM S columns [0,64) and [64,128), O at [128,384) of a
-// 512-column allocation; two P tiles in shared memory), so the tensor core computes S(j+2) and
-// P.V(j) while the softmax warps turn S(j+1) into probabilities.
+// Two-SM design (tcgen05 cta_group::2): a cluster of two CTAs runs one kv head for two adjacent
+// 32-token query tiles. The 4 GQA heads of the kv head are stacked into each CTA's 128 rows
+// (row r = token r/4, head r%4), so the pair's MMAs have M = 256 and every K/V tile serves 64
+// tokens x 4 heads. The leader CTA issues S = Q K^T (M256 N128 K256) and O += P V (M256 N256
+// K128) for both; each CTA stages its own Q, 64 of the tile's 128 keys and 128 of the 256 value
+// dims, so each SM fetches half of every K/V tile. Per CTA (352 threads): warps 0-7 softmax +
+// epilogue (two warps per TMEM lane quarter, splitting key columns and O dims), warp 8 the MMA
+// issuer (leader only), warp 9 the Q/K TMA producer, warp 10 the V producer. TMEM: O in columns
+// [0,256), two S tiles in [256,512); P(j) is written over the first 64 columns of S(j).
 #include <cuda.h>
 
 #include "pgc_common.cuh"
@@ -55,29 +54,8 @@ namespace {
 
 constexpr int kBM = 128;           // rows = 32 tokens x 4 heads
 constexpr int kTokTile = 32;
-constexpr int kBN = 64;            // keys per tile (4 pages)
-constexpr int kThreadsP = 224;
-constexpr int kQBytes = kBM * kHeadDim * 2;      // 64 KiB: [4 dim blocks][128 rows][128 B]
-constexpr int kKVTileBytes = kBN * kHeadDim * 2;  // 32 KiB: [4 dim blocks][64 keys][128 B]
-constexpr int kPBytes = kBM * kBN * 2;            // 16 KiB: [128 rows][128 B]
-constexpr int kStagesP = 2;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;
-constexpr uint32_t kTmemO = 128;
 constexpr float kLazyRescale = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
-
-struct SmemP {
-    static constexpr int kQ = 0;
-    static constexpr int kK = kQ + kQBytes;                   // K ring [2]
-    static constexpr int kV = kK + kStagesP * kKVTileBytes;   // V ring [2]
-    static constexpr int kP = kV + kStagesP * kKVTileBytes;   // P [2]
-    static constexpr int kBar = kP + 2 * kPBytes;
-    // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], p_free[2]
-    static constexpr int kNumBars = 15;
-    static constexpr int kTmemSlot = kBar + kNumBars * 8;
-    static constexpr int kBytes = kTmemSlot + 16;
-};
-constexpr int kSmemBytesP = SmemP::kBytes + 1024;
 
 struct PrefillParams {
     const int32_t *block_table;
@@ -103,22 +81,6 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
 __host__ __device__ constexpr uint32_t umma_idesc(int m, int n, bool a_mn_major, bool b_mn_major) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
            ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 ::"r"(smem_u32(bar))
-                 : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -171,16 +133,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         : "memory");
 }
 
-// 3-D tiled TMA load (Q tile: 64 dims x 4 heads x 32 tokens).
-__device__ __forceinline__ void tma_load_3d(void *smem_dst, const void *tmap, int32_t x, int32_t y,
-                                            int32_t z, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
-        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-        : "memory");
-}
-
 // Bounded wait that also gives up as soon as another role of the CTA has recorded a timeout.
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
                                               int where) {
@@ -200,304 +152,6 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
         }
     }
 }
-
-__global__ void __launch_bounds__(kThreadsP, 1)
-    prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                   const __grid_constant__ CUtensorMap tmv, const PrefillParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ int abort_flag_s;
-
-    const int qt = blockIdx.x;
-    const int kvh = blockIdx.y;
-    const int T = p.chunk_len, P = p.prefix_len;
-    const int tok0 = qt * kTokTile;
-    const int t_last = min(tok0 + kTokTile - 1, T - 1);
-    const int n_keys = P + t_last + 1;  // keys any row of this tile may see
-    const int n_tiles = (n_keys + kBN - 1) / kBN;
-    const int total_keys = P + T;       // keys present in the cache
-    // this CTA's share of the key tiles (split z of nsplit; the host keeps every share >= 1)
-    const int tb = (int)((int64_t)n_tiles * blockIdx.z / p.nsplit);
-    const int n_loc = (int)((int64_t)n_tiles * (blockIdx.z + 1) / p.nsplit) - tb;
-
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SmemP::kBar);
-    uint64_t *q_full = bars + 0;
-    uint64_t *k_full = bars + 1;   // [2]
-    uint64_t *k_empty = bars + 3;  // [2]
-    uint64_t *v_full = bars + 5;   // [2]
-    uint64_t *v_empty = bars + 7;  // [2]
-    uint64_t *s_full = bars + 9;   // [2] S buffer b holds a finished S tile
-    uint64_t *p_full = bars + 11;  // [2] P buffer b written (128 arrivals)
-    uint64_t *p_free = bars + 13;  // [2] P.V that read P buffer b has completed
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SmemP::kTmemSlot);
-    volatile int *abort_flag = &abort_flag_s;
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        abort_flag_s = 0;
-        mbar_init(q_full, 1);
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&k_full[b], 1);
-            mbar_init(&k_empty[b], 1);
-            mbar_init(&v_full[b], 1);
-            mbar_init(&v_empty[b], 1);
-            mbar_init(&s_full[b], 1);
-            mbar_init(&p_full[b], kBM);
-            mbar_init(&p_free[b], 1);
-        }
-        fence_mbar_init();
-    }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(smem_u32(tmem_slot)), "r"(kTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    uint8_t *q_s = smem + SmemP::kQ;
-
-    if (warp == 5 || warp == 6) {
-        // ------------------------------------------------------------ TMA producers
-        // warp 5 streams Q and the K tiles, warp 6 the V tiles; each ring slot is refilled as
-        // soon as the MMA that read it has completed (S for K, P.V for V).
-        if (lane == 0) {
-            const bool is_k = warp == 5;
-            const CUtensorMap *tm = is_k ? &tmk : &tmv;
-            tma_prefetch_desc(tm);
-            // every q-tile CTA of a kv head streams the same K/V: ask L2 to keep it
-            const uint64_t pol = l2_policy_evict_last();
-            if (is_k) {
-                tma_prefetch_desc(&tmq);
-                mbar_arrive_expect_tx(q_full, kQBytes);
-                for (int c = 0; c < 4; ++c)
-                    tma_load_3d(q_s + c * (kBM * 128), &tmq, c * 64, kvh * kGroup, tok0, q_full);
-            }
-            uint64_t *full = is_k ? k_full : v_full;
-            uint64_t *empty = is_k ? k_empty : v_empty;
-            uint8_t *ring = smem + (is_k ? SmemP::kK : SmemP::kV);
-            for (int j = 0; j < n_loc; ++j) {
-                const int b = j & 1;
-                if (j >= 2 && !wait_or_abort(&empty[b], ((j >> 1) - 1) & 1, abort_flag, 1)) break;
-                const int key0 = (tb + j) * kBN;
-                int npg = 0;
-                for (int pp = 0; pp < kBN / kPage; ++pp)
-                    if (key0 + pp * kPage < total_keys) ++npg;
-                mbar_arrive_expect_tx(&full[b], (uint32_t)npg * kPage * kHeadDim * 2);
-                uint8_t *tile = ring + b * kKVTileBytes;
-                for (int pp = 0; pp < npg; ++pp) {
-                    int page = p.block_table[(key0 >> 4) + pp];
-                    if (page < 0 || page >= p.num_pages) {
-                        record_error(&g_prefill_err, kErrPageOutOfRange, page);
-                        page = 0;
-                    }
-                    const int row = (page * kNumKvHeads + kvh) * kPage;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        tma_load_2d(tile + c * (kBN * 128) + pp * 2048, tm, c * 64, row, &full[b], pol);
-                }
-            }
-        }
-    } else if (warp == 4) {
-        // ------------------------------------------------------------ MMA issuer
-        // Issue order S0 S1 PV0 S2 PV1 S3 ...: S(j+2) and P.V(j) run while the softmax
-        // warps work on S(j+1).
-        if (lane == 0) {
-            constexpr uint32_t idesc_s = umma_idesc(kBM, kBN, false, false);
-            constexpr uint32_t idesc_o = umma_idesc(kBM, kHeadDim, false, true);
-            const uint32_t q_addr = smem_u32(q_s);
-            auto issue_s = [&](int jj) -> bool {
-                const int b = jj & 1;
-                if (!wait_or_abort(&k_full[b], (jj >> 1) & 1, abort_flag, 3)) return false;
-                tc_fence_after();
-                const uint32_t k_addr = smem_u32(smem + SmemP::kK + b * kKVTileBytes);
-#pragma unroll
-                for (int kk = 0; kk < kHeadDim / 16; ++kk)
-                    umma_f16(tmem + kTmemS + b * kBN,
-                             umma_desc(q_addr + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024),
-                             umma_desc(k_addr + (kk >> 2) * (kBN * 128) + (kk & 3) * 32, 16, 1024),
-                             idesc_s, kk > 0 ? 1u : 0u);
-                umma_commit(&k_empty[b]);
-                umma_commit(&s_full[b]);
-                return true;
-            };
-            bool ok = wait_or_abort(q_full, 0, abort_flag, 2);
-            if (ok) ok = issue_s(0);
-            if (ok && n_loc > 1) ok = issue_s(1);
-            for (int j = 0; ok && j < n_loc; ++j) {
-                const int b = j & 1;
-                if (!wait_or_abort(&p_full[b], (j >> 1) & 1, abort_flag, 4) ||
-                    !wait_or_abort(&v_full[b], (j >> 1) & 1, abort_flag, 5)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t p_addr = smem_u32(smem + SmemP::kP + b * kPBytes);
-                const uint32_t v_addr = smem_u32(smem + SmemP::kV + b * kKVTileBytes);
-#pragma unroll
-                for (int kk = 0; kk < kBN / 16; ++kk)
-                    umma_f16(tmem + kTmemO, umma_desc(p_addr + kk * 32, 16, 1024),
-                             umma_desc(v_addr + kk * 2048, kBN * 128, 1024), idesc_o,
-                             (j > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&v_empty[b]);
-                umma_commit(&p_free[b]);
-                if (j + 2 < n_loc) ok = issue_s(j + 2);
-            }
-        }
-    } else {
-        // ------------------------------------------------------------ softmax + epilogue
-        const int r = threadIdx.x;  // accumulator row = TMEM lane
-        const int t = tok0 + r / kGroup;
-        const int g = r % kGroup;
-        const bool row_ok = t < T;
-        const int vis = P + t;  // keys c <= vis are visible
-        const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-        float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (int j = 0; j < n_loc; ++j) {
-            const int b = j & 1;
-            if (!wait_or_abort(&s_full[b], (j >> 1) & 1, abort_flag, 6)) { ok = false; break; }
-            tc_fence_after();
-            float sv[64];
-            {
-                float a[32], c2[32];
-                tmem_ld32(tmem + lane_addr + kTmemS + b * kBN, a);
-                tmem_ld32(tmem + lane_addr + kTmemS + b * kBN + 32, c2);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) { sv[i] = a[i]; sv[32 + i] = c2[i]; }
-            }
-            const int key0 = (tb + j) * kBN;
-            float mx = -INFINITY;
-            if (key0 + kBN - 1 <= vis && row_ok) {  // tile entirely visible: no per-key test
-#pragma unroll
-                for (int i = 0; i < kBN; ++i) {
-                    sv[i] *= p.scale_log2;
-                    mx = fmaxf(mx, sv[i]);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < kBN; ++i) {
-                    sv[i] = (row_ok && key0 + i <= vis) ? sv[i] * p.scale_log2 : -INFINITY;
-                    mx = fmaxf(mx, sv[i]);
-                }
-            }
-            const float m_new = fmaxf(m, mx);
-            float corr = 1.f;
-            if (m_new > m + kLazyRescale) {  // also true the first time a row sees a key
-                corr = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
-                m = m_new;
-            }
-            const float m_use = (m == -INFINITY) ? 0.f : m;
-            float ps = 0.f;
-#pragma unroll
-            for (int i = 0; i < kBN; ++i) {
-                sv[i] = fast_exp2(sv[i] - m_use);
-                ps += sv[i];
-            }
-            l = l * corr + ps;
-            if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-                // O must be stable: wait for P.V(j-1), the last MMA writing it
-                if (!wait_or_abort(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 7)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-#pragma unroll 1
-                for (int cc = 0; cc < kHeadDim / 32; ++cc) {
-                    float o[32];
-                    tmem_ld32(tmem + lane_addr + kTmemO + cc * 32, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= corr;
-                    tmem_st32(tmem + lane_addr + kTmemO + cc * 32, o);
-                }
-                tmem_wait_st();
-            }
-            // P buffer b is free once P.V(j-2), the previous reader, has completed
-            if (j >= 2 && !wait_or_abort(&p_free[b], ((j >> 1) - 1) & 1, abort_flag, 10)) {
-                ok = false;
-                break;
-            }
-            uint8_t *p_s = smem + SmemP::kP + b * kPBytes;
-#pragma unroll
-            for (int ch = 0; ch < kBN / 8; ++ch) {
-                uint4 v;
-                v.x = pack_bf16x2(sv[ch * 8 + 0], sv[ch * 8 + 1]);
-                v.y = pack_bf16x2(sv[ch * 8 + 2], sv[ch * 8 + 3]);
-                v.z = pack_bf16x2(sv[ch * 8 + 4], sv[ch * 8 + 5]);
-                v.w = pack_bf16x2(sv[ch * 8 + 6], sv[ch * 8 + 7]);
-                *reinterpret_cast<uint4 *>(p_s + r * 128 + ((ch ^ (r & 7)) << 4)) = v;
-            }
-            if (key0 + kBN > total_keys) {
-                // Keys past the cache end (stale slots, or pages not loaded) get zero V rows so
-                // that a NaN pattern cannot reach the P.V product through a zero probability.
-                if (!wait_or_abort(&v_full[b], (j >> 1) & 1, abort_flag, 8)) { ok = false; break; }
-                uint8_t *vt = smem + SmemP::kV + b * kKVTileBytes;
-                const int first = total_keys - key0;
-                const int nz = (kBN - first) * 4 * 8;  // rows x 4 dim blocks x 8 units of 16 B
-                for (int i = r; i < nz; i += kBM) {
-                    const int row = first + i / 32;
-                    const int u = i % 32;
-                    *reinterpret_cast<uint4 *>(vt + (u >> 3) * (kBN * 128) + row * 128 + (u & 7) * 16) =
-                        make_uint4(0, 0, 0, 0);
-                }
-            }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(&p_full[b]);
-        }
-        const int jl = n_loc - 1;
-        if (ok && wait_or_abort(&p_free[jl & 1], (jl >> 1) & 1, abort_flag, 9)) {
-            tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            const int64_t orow = (int64_t)t * kNumQHeads + kvh * kGroup + g;
-            uint16_t *dst = p.out + orow * kHeadDim;
-            float *part = p.nsplit > 1
-                              ? p.ws + ((int64_t)blockIdx.z * T * kNumQHeads + orow) * kPartial
-                              : nullptr;
-            if (part != nullptr && row_ok) {
-                part[0] = (m == -INFINITY) ? -INFINITY : m * kLn2;  // natural-log units
-                part[1] = l;
-            }
-#pragma unroll 1
-            for (int cc = 0; cc < kHeadDim / 32; ++cc) {
-                float o[32];
-                tmem_ld32(tmem + lane_addr + kTmemO + cc * 32, o);
-                tmem_wait_ld();
-                if (!row_ok) continue;
-                if (part != nullptr) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 2)
-                        *reinterpret_cast<float2 *>(part + 2 + cc * 32 + i) = make_float2(o[i], o[i + 1]);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
-                        uint4 v;
-                        v.x = pack_bf16x2(o[i] * inv, o[i + 1] * inv);
-                        v.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
-                        v.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
-                        v.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
-                        *reinterpret_cast<uint4 *>(dst + cc * 32 + i) = v;
-                    }
-                }
-            }
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(kTmemCols)
-                     : "memory");
-    }
-}
-
 
 // ---------------------------------------------------------------- two-SM (cta_group::2) helpers
 __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
@@ -916,6 +570,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                 tmem_ld32(tmem + lane_addr + kTS + b * kBNp + h * 64, a);
                 tmem_ld32(tmem + lane_addr + kTS + b * kBNp + h * 64 + 32, c2);
                 tmem_wait_ld();
+                if (threadIdx.x == 0) PF_TRACE(5, j);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) { sv[i] = a[i]; sv[32 + i] = c2[i]; }
             }
@@ -939,6 +594,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
             // both halves have read S tile b before either overwrites it with P
             asm volatile("bar.sync %0, 64;" ::"r"(1 + qd) : "memory");
             mx = fmaxf(mx, red[(b * 2 + (h ^ 1)) * kBM + r]);
+            if (threadIdx.x == 0) PF_TRACE(6, j);
             const float m_new = fmaxf(m, mx);
             float corr = 1.f;
             if (m_new > m + kLazyRescale) {
@@ -956,6 +612,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                 pw[i >> 1] = pack_bf16x2(a0, a1);
             }
             l = l * corr + ps;
+            if (threadIdx.x == 0) PF_TRACE(7, j);
             if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
                 if (!wait_or_abort(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 7)) {
                     ok = false;
@@ -1046,10 +703,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
 // and never more shares than the smallest CTA has key tiles); the shares are merged by
 // merge_kernel.
 int prefill_nsplit(int prefix_len, int chunk_len, int sm_count) {
+    // Work items are CTA pairs x key-range splits; sm_count / 2 pairs are resident at once.
+    // Measured: once the pairs cover the GPU, splitting to fill the last wave does not help
+    // (the K/V delivery rate of the whole chip, not SM occupancy, is then the limit), so the
+    // key range is split only when there are fewer pairs than resident slots, to at most 8
+    // shares and never more shares than the smallest pair has 128-key tiles.
     const int qtiles = (chunk_len + kTokTile - 1) / kTokTile;
-    const int ctas = ((qtiles + 1) / 2) * 2 * kNumKvHeads;  // CTA pairs
+    const int pairs = ((qtiles + 1) / 2) * kNumKvHeads;
+    const int slots = sm_count / 2 > 0 ? sm_count / 2 : 1;
     const int min_tiles = (prefix_len + (chunk_len < kTokTile ? chunk_len : kTokTile) + 127) / 128;
-    int ns = sm_count / ctas;
+    int ns = slots / pairs;
     if (ns > 8) ns = 8;
     if (ns > min_tiles) ns = min_tiles;
     return ns < 1 ? 1 : ns;
@@ -1065,13 +728,8 @@ cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUten
                            const uint16_t *v_pages, int64_t num_pages, const int32_t *block_table, int prefix_len,
                            int chunk_len, float scale, uint16_t *out, void *workspace,
                            int sm_count, cudaStream_t stream) {
-#ifdef PGC_PREFILL_ONE_SM
-    auto kern = prefill_kernel;
-    const int smem_bytes = kSmemBytesP, threads = kThreadsP, xmul = 1;
-#else
     auto kern = prefill_pair_kernel;
     const int smem_bytes = pair::Smem2::kBytes, threads = pair::kThreads, xmul = 2;
-#endif
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);

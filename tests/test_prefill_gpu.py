@@ -68,7 +68,7 @@ def test_prefill_config2_shape(cuda, oracle):
 def test_prefill_workspace_rules(cuda):
     import torch
     from peregrine_b200.capi import PgcError
-    assert cuda.prefill_workspace_bytes(24576, 1600) == 0  # config 2's grid covers the SMs
+    assert cuda.prefill_workspace_bytes(24576, 1600) == 0  # config 2's pairs cover the GPU
     P, T = 24576, 96  # 12 CTAs: the key range is split, partials need a workspace
     nbytes = cuda.prefill_workspace_bytes(P, T)
     assert nbytes > 0 and nbytes % (T * NQ * 258 * 4) == 0
