@@ -58,7 +58,9 @@ enum pgc_status {
     PGC_ERR_ALIGN = -5,     /* a pointer or size lacks the required alignment */
     PGC_ERR_DEVICE = -6,    /* current device is not sm_100 */
     PGC_ERR_TIMEOUT = -7,   /* a bounded device wait gave up (reported by pgc_device_error) */
-    PGC_ERR_CONTEXT = -8    /* length outside (0, PGC_MAX_CONTEXT_TOKENS] */
+    PGC_ERR_CONTEXT = -8,   /* length outside (0, PGC_MAX_CONTEXT_TOKENS] */
+    PGC_ERR_FILE = -9,      /* file missing, unreadable or not writable */
+    PGC_ERR_FORMAT = -10    /* prefix-state file fails validation (wrong model, size, ...) */
 };
 
 /* Status text for an error code (static storage). */
@@ -287,6 +289,60 @@ int pgc_zero_regions(const pgc_region *regions_host, int n, void *stream);
  * src/server/decode_loop.zig:216-258,295-311. */
 int pgc_rollback(const int32_t *accept, int32_t *seq_lens, int seq_index, int reject_tokens,
                  const pgc_region *regions_host, int n, void *stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Prefix-state snapshot file (format v3 of src/server/prefix_persist.zig:31-137)
+ * ------------------------------------------------------------------------------------- */
+
+/* Byte offsets of every section of a v3 file holding `token_count` tokens. Linear layers are
+ * numbered in model order (24: conv f32 [3][8192], recurrent f32 [32][128][128]); full layers
+ * too (8: K runs [4][count][256] bf16 = a dense K of stride count, V runs [4][256][count] bf16
+ * = a dense V of stride count). Replaces expectedFileBytes / fullCacheRuns
+ * (prefix_persist.zig:64-137). */
+typedef struct pgc_prefix_layout {
+    uint64_t token_count;
+    uint64_t tokens;      /* u32 [count] */
+    uint64_t conv[24];
+    uint64_t recur[24];
+    uint64_t k_runs[8];
+    uint64_t v_runs[8];
+    uint64_t hidden;      /* bf16 [count][4096] */
+    uint64_t total_bytes; /* exact file size */
+} pgc_prefix_layout;
+
+typedef struct pgc_prefix_info {
+    uint64_t token_count;
+    uint32_t next_token;
+    uint32_t next_token_valid;
+    uint32_t hidden_valid;
+    uint64_t file_bytes;
+} pgc_prefix_info;
+
+int pgc_prefix_file_layout(uint64_t token_count, pgc_prefix_layout *out);
+
+/* Validates a v3 file without reading its payload: magic, version, dtype, model fingerprint,
+ * flags, cached next token < vocab, 0 < token_count <= max_tokens and the exact file size.
+ * PGC_ERR_FILE when it cannot be opened, PGC_ERR_FORMAT when it must be ignored (the caller
+ * then cold-prefills). Replaces the checks of load() (src/server/prefix_persist.zig:329-356). */
+int pgc_prefix_file_inspect(const char *path, uint64_t model_fingerprint, uint64_t vocab,
+                            uint64_t max_tokens, pgc_prefix_info *info);
+
+/* Validates, then reads the whole file into `image` (ideally pinned host memory: the restore
+ * kernels then read it directly). Section offsets from pgc_prefix_file_layout. */
+int pgc_prefix_file_read(const char *path, uint64_t model_fingerprint, uint64_t vocab,
+                         uint64_t max_tokens, void *image, uint64_t image_bytes,
+                         pgc_prefix_info *info);
+
+/* Writes the 48-byte header into a file image whose sections the caller has filled (token
+ * ids, linear states, pgc_kv_snapshot_dense into the K/V runs with dst_stride = count, hidden
+ * rows). */
+int pgc_prefix_file_header(void *image, uint64_t image_bytes, uint64_t model_fingerprint,
+                           uint64_t token_count, uint32_t next_token, int next_token_valid,
+                           int hidden_valid);
+
+/* Atomically replaces `path` with the image (temporary file, fsync, rename), as save() does
+ * (src/server/prefix_persist.zig:255-326). */
+int pgc_prefix_file_write(const char *path, const void *image, uint64_t image_bytes);
 
 #ifdef __cplusplus
 }

@@ -31,7 +31,7 @@ APPEND_PREFILL = 1
 STATUS = {
     0: "PGC_OK", -1: "PGC_ERR_INVALID", -2: "PGC_ERR_BOUNDS", -3: "PGC_ERR_WORKSPACE",
     -4: "PGC_ERR_CUDA", -5: "PGC_ERR_ALIGN", -6: "PGC_ERR_DEVICE", -7: "PGC_ERR_TIMEOUT",
-    -8: "PGC_ERR_CONTEXT",
+    -8: "PGC_ERR_CONTEXT", -9: "PGC_ERR_FILE", -10: "PGC_ERR_FORMAT",
 }
 
 
@@ -43,6 +43,19 @@ class PgcError(RuntimeError):
 
 class Region(C.Structure):
     _fields_ = [("dst", C.c_void_p), ("src", C.c_void_p), ("bytes", C.c_uint64)]
+
+
+class PrefixLayout(C.Structure):
+    _fields_ = [("token_count", C.c_uint64), ("tokens", C.c_uint64),
+                ("conv", C.c_uint64 * 24), ("recur", C.c_uint64 * 24),
+                ("k_runs", C.c_uint64 * 8), ("v_runs", C.c_uint64 * 8),
+                ("hidden", C.c_uint64), ("total_bytes", C.c_uint64)]
+
+
+class PrefixInfo(C.Structure):
+    _fields_ = [("token_count", C.c_uint64), ("next_token", C.c_uint32),
+                ("next_token_valid", C.c_uint32), ("hidden_valid", C.c_uint32),
+                ("file_bytes", C.c_uint64)]
 
 
 P = C.c_void_p
@@ -74,6 +87,11 @@ SIGNATURES = {
     "pgc_copy_regions": (I32, [C.POINTER(Region), I32, P]),
     "pgc_zero_regions": (I32, [C.POINTER(Region), I32, P]),
     "pgc_rollback": (I32, [P, P, I32, I32, C.POINTER(Region), I32, P]),
+    "pgc_prefix_file_layout": (I32, [U64, C.POINTER(PrefixLayout)]),
+    "pgc_prefix_file_inspect": (I32, [C.c_char_p, U64, U64, U64, C.POINTER(PrefixInfo)]),
+    "pgc_prefix_file_read": (I32, [C.c_char_p, U64, U64, U64, P, U64, C.POINTER(PrefixInfo)]),
+    "pgc_prefix_file_header": (I32, [P, U64, U64, U64, C.c_uint32, I32, I32]),
+    "pgc_prefix_file_write": (I32, [C.c_char_p, P, U64]),
 }
 
 _lib = None
@@ -256,3 +274,39 @@ def zero_regions(pairs, stream=None) -> None:
 def rollback(accept, seq_lens, seq_index, reject_tokens, pairs, stream=None) -> None:
     check(lib().pgc_rollback(_ptr(accept), _ptr(seq_lens), seq_index, reject_tokens,
                              _regions(pairs), len(pairs), _stream(stream)), "pgc_rollback")
+
+
+# ----------------------------------------------------------------------------- prefix-state file
+
+def prefix_file_layout(token_count: int) -> PrefixLayout:
+    lay = PrefixLayout()
+    check(lib().pgc_prefix_file_layout(token_count, C.byref(lay)), "pgc_prefix_file_layout")
+    return lay
+
+
+def prefix_file_inspect(path, fingerprint: int, vocab: int, max_tokens: int) -> PrefixInfo:
+    info = PrefixInfo()
+    check(lib().pgc_prefix_file_inspect(str(path).encode(), fingerprint, vocab, max_tokens,
+                                        C.byref(info)), "pgc_prefix_file_inspect")
+    return info
+
+
+def prefix_file_read(path, fingerprint: int, vocab: int, max_tokens: int, image_ptr: int,
+                     image_bytes: int) -> PrefixInfo:
+    info = PrefixInfo()
+    check(lib().pgc_prefix_file_read(str(path).encode(), fingerprint, vocab, max_tokens,
+                                     image_ptr, image_bytes, C.byref(info)), "pgc_prefix_file_read")
+    return info
+
+
+def prefix_file_header(image_ptr: int, image_bytes: int, fingerprint: int, token_count: int,
+                       next_token: int = 0, next_token_valid: bool = False,
+                       hidden_valid: bool = False) -> None:
+    check(lib().pgc_prefix_file_header(image_ptr, image_bytes, fingerprint, token_count,
+                                       next_token, int(next_token_valid), int(hidden_valid)),
+          "pgc_prefix_file_header")
+
+
+def prefix_file_write(path, image_ptr: int, image_bytes: int) -> None:
+    check(lib().pgc_prefix_file_write(str(path).encode(), image_ptr, image_bytes),
+          "pgc_prefix_file_write")

@@ -68,6 +68,7 @@ constexpr int kDenseTile = 32;  // tokens per CTA
 // V is value-dim-major in the dense layout and token-major in the pages, so it is
 // transposed through shared memory: coalesced 64-byte runs on the dense side, whole 512-byte
 // rows on the page side.
+template <typename KV>
 __global__ void __launch_bounds__(256)
     kv_dense_kernel(bool restore, uint16_t *dk, uint16_t *dv, int64_t dstride, int64_t dtok,
                     uint16_t *kp, uint16_t *vp, int64_t num_pages, const int32_t *table,
@@ -81,13 +82,15 @@ __global__ void __launch_bounds__(256)
     if (tid < kDenseTile) rows[tid] = tid < n ? paged_row(table, n_table, num_pages, ptok + base + tid, kvh) : -1;
     __syncthreads();
 
-    // K: 32 tokens x 32 uint4
-    for (int i = tid; i < n * 32; i += 256) {
-        const int tt = i >> 5, u = i & 31;
+    // K: 32 tokens x one 512-byte row each, in units of KV (16 B when the dense side is
+    // 16-byte aligned; a file image's runs may only be 4- or 2-byte aligned)
+    constexpr int kUnits = kHeadDim * 2 / (int)sizeof(KV);
+    for (int i = tid; i < n * kUnits; i += 256) {
+        const int tt = i / kUnits, u = i % kUnits;
         const int64_t pr = rows[tt];
         if (pr < 0) continue;
-        uint4 *prow = reinterpret_cast<uint4 *>(kp + pr);
-        uint4 *drow = reinterpret_cast<uint4 *>(dk + ((int64_t)kvh * dstride + dtok + base + tt) * kHeadDim);
+        KV *prow = reinterpret_cast<KV *>(kp + pr);
+        KV *drow = reinterpret_cast<KV *>(dk + ((int64_t)kvh * dstride + dtok + base + tt) * kHeadDim);
         if (restore) prow[u] = drow[u];
         else drow[u] = prow[u];
     }
@@ -210,9 +213,19 @@ cudaError_t launch_kv_dense(bool restore, uint16_t *dense_k, uint16_t *dense_v,
                             cudaStream_t stream) {
     if (count == 0) return cudaSuccess;
     dim3 grid((unsigned)((count + kDenseTile - 1) / kDenseTile), kNumKvHeads);
-    kv_dense_kernel<<<grid, 256, 0, stream>>>(restore, dense_k, dense_v, dense_stride, dense_token,
-                                              k_pages, v_pages, num_pages, table, n_table,
-                                              page_token, count);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(dense_k);
+    if (a % 16 == 0)
+        kv_dense_kernel<uint4><<<grid, 256, 0, stream>>>(restore, dense_k, dense_v, dense_stride,
+                                                         dense_token, k_pages, v_pages, num_pages,
+                                                         table, n_table, page_token, count);
+    else if (a % 4 == 0)
+        kv_dense_kernel<uint32_t><<<grid, 256, 0, stream>>>(restore, dense_k, dense_v, dense_stride,
+                                                            dense_token, k_pages, v_pages, num_pages,
+                                                            table, n_table, page_token, count);
+    else
+        kv_dense_kernel<uint16_t><<<grid, 256, 0, stream>>>(restore, dense_k, dense_v, dense_stride,
+                                                            dense_token, k_pages, v_pages, num_pages,
+                                                            table, n_table, page_token, count);
     return cudaGetLastError();
 }
 

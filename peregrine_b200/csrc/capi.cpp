@@ -163,6 +163,8 @@ const char *pgc_status_string(int status) {
         case PGC_ERR_DEVICE: return "current device is not sm_100";
         case PGC_ERR_TIMEOUT: return "bounded device wait timed out";
         case PGC_ERR_CONTEXT: return "invalid context length";
+        case PGC_ERR_FILE: return "file missing or not accessible";
+        case PGC_ERR_FORMAT: return "prefix-state file failed validation";
         default: return "unknown status";
     }
 }
@@ -382,7 +384,8 @@ static int dense_checks(const void *kd, const void *vd, int64_t stride, int64_t 
     if (!kd || !vd || !kp || !vp || !table) return PGC_ERR_INVALID;
     if (tok + count > stride) return PGC_ERR_BOUNDS;
     if ((ptok + count + PGC_PAGE_TOKENS - 1) / PGC_PAGE_TOKENS > n_table) return PGC_ERR_BOUNDS;
-    if (!al16(kd) || !al16(kp) || !al16(vp)) return PGC_ERR_ALIGN;
+    // the dense side may be a file image (2-byte aligned bf16 runs); pools are 16-byte aligned
+    if (((uintptr_t)kd & 1u) || ((uintptr_t)vd & 1u) || !al16(kp) || !al16(vp)) return PGC_ERR_ALIGN;
     return PGC_OK;
 }
 
