@@ -60,7 +60,8 @@ enum pgc_status {
     PGC_ERR_TIMEOUT = -7,   /* a bounded device wait gave up (reported by pgc_device_error) */
     PGC_ERR_CONTEXT = -8,   /* length outside (0, PGC_MAX_CONTEXT_TOKENS] */
     PGC_ERR_FILE = -9,      /* file missing, unreadable or not writable */
-    PGC_ERR_FORMAT = -10    /* prefix-state file fails validation (wrong model, size, ...) */
+    PGC_ERR_FORMAT = -10,   /* prefix-state file fails validation (wrong model, size, ...) */
+    PGC_ERR_CAPACITY = -11  /* page pool or linear-state slots exhausted after eviction */
 };
 
 /* Status text for an error code (static storage). */
@@ -343,6 +344,124 @@ int pgc_prefix_file_header(void *image, uint64_t image_bytes, uint64_t model_fin
 /* Atomically replaces `path` with the image (temporary file, fsync, rename), as save() does
  * (src/server/prefix_persist.zig:255-326). */
 int pgc_prefix_file_write(const char *path, const void *image, uint64_t image_bytes);
+
+/* ---------------------------------------------------------------------------------------
+ * Page pool and page-refcounted prefix cache (host side, no device work).
+ *
+ * Replaces the resident prompt-prefix cache (src/server/prefix_state_cache.zig:21-567). The
+ * reference entry owns a private model state and every hit or store copies KV rows
+ * (state.zig:124-230); here every KV page of every full layer, and the MTP hidden-row pool, is
+ * indexed by one page id, an entry is a list of page ids, and sharing is a refcount:
+ *   hit:    pgc_prefix_cache_fork -> the request's block table starts with the entry's pages;
+ *           before writing into a page it does not own alone (the partial page at the end of a
+ *           match) the request calls pgc_page_pool_make_writable and copies that one page on
+ *           the device (pgc_copy_regions over each per-page pool);
+ *   store:  pgc_prefix_cache_store adopts the work sequence's pages (no KV copy);
+ *   linear state (recurrent + conv) is not paged: each entry owns a state slot and the caller
+ *           copies it where the reference does (copy_linear_state reports when).
+ * The policy is the reference's: token-level longest-prefix match, reserved-token budget with
+ * capacity max(len, prefill chunk), LRU eviction of unpinned entries, entry indexes that shift
+ * down when an earlier entry is removed (a pgc_match is valid until the next mutation).
+ * Constructors return NULL on failure (bridge.h convention); one thread per cache.
+ * ------------------------------------------------------------------------------------- */
+typedef struct pgc_page_pool pgc_page_pool;
+typedef struct pgc_prefix_cache pgc_prefix_cache;
+
+/* The reference's Match (prefix_state_cache.zig:16-19); index -1 = no match. */
+typedef struct pgc_match {
+    int64_t index;
+    int64_t len;
+} pgc_match;
+
+/* Cache.Stats (prefix_state_cache.zig:200-229) plus resident/pinned/active/trie counters. */
+typedef struct pgc_prefix_stats {
+    uint64_t hits, misses, hit_tokens, computed_tokens;
+    uint64_t reserved_tokens, resident_tokens, max_tokens;
+    uint64_t entry_count, pinned_count, evictions, trie_nodes;
+    int64_t active_index;
+} pgc_prefix_stats;
+
+typedef struct pgc_prefix_entry {
+    uint64_t token_count;
+    int64_t page_count;
+    uint64_t capacity;      /* reserved tokens */
+    int32_t state_slot;     /* linear-state slot owned by the entry */
+    int32_t pinned, hidden_valid, next_token_valid;
+    uint32_t next_token;
+    uint64_t last_access, hits;
+} pgc_prefix_entry;
+
+pgc_page_pool *pgc_page_pool_create(int32_t num_pages);
+void pgc_page_pool_destroy(pgc_page_pool *pool);
+/* n fresh pages with one reference each; PGC_ERR_CAPACITY (nothing taken) when fewer are free. */
+int pgc_page_pool_alloc(pgc_page_pool *pool, int32_t n, int32_t *pages_out);
+int pgc_page_pool_retain(pgc_page_pool *pool, const int32_t *pages, int32_t n);
+/* Drops one reference per listed page; a page reaching 0 returns to the free list. */
+int pgc_page_pool_release(pgc_page_pool *pool, const int32_t *pages, int32_t n);
+int32_t pgc_page_pool_refcount(const pgc_page_pool *pool, int32_t page);
+int32_t pgc_page_pool_free_pages(const pgc_page_pool *pool);
+/* Copy-on-write for table[slot]: if the page has other holders, a fresh page replaces it in
+ * the table (this holder's reference moves to it) and *src != *dst names the device copy to
+ * issue before writing; otherwise *src == *dst and nothing is to be copied. */
+int pgc_page_pool_make_writable(pgc_page_pool *pool, int32_t *table, int32_t slot,
+                                int32_t *src_page, int32_t *dst_page);
+
+/* Cache.init (prefix_state_cache.zig:312-320) over `pool`, with `state_slots` linear-state
+ * slots. The pool must outlive the cache. */
+pgc_prefix_cache *pgc_prefix_cache_create(pgc_page_pool *pool, int32_t page_tokens,
+                                          uint64_t max_tokens, uint64_t prefill_chunk_tokens,
+                                          int32_t state_slots);
+void pgc_prefix_cache_destroy(pgc_prefix_cache *cache);
+void pgc_prefix_cache_clear_all(pgc_prefix_cache *cache);
+void pgc_prefix_cache_enable_hidden_tracking(pgc_prefix_cache *cache);
+/* findPrefix: 1 and the longest cached prefix of the prompt, or 0 (out->index = -1). */
+int pgc_prefix_cache_find(const pgc_prefix_cache *cache, const uint32_t *prompt, uint64_t n,
+                          pgc_match *out);
+/* containsPromptPrefix: 1 when an entry holds exactly prompt[0, prefix_len). */
+int pgc_prefix_cache_contains(const pgc_prefix_cache *cache, const uint32_t *prompt, uint64_t n,
+                              uint64_t prefix_len);
+void pgc_prefix_cache_touch(pgc_prefix_cache *cache, pgc_match match);
+void pgc_prefix_cache_record_hit(pgc_prefix_cache *cache, uint64_t reused_tokens);
+void pgc_prefix_cache_record_miss(pgc_prefix_cache *cache);
+void pgc_prefix_cache_record_computed(pgc_prefix_cache *cache, uint64_t tokens);
+int pgc_prefix_cache_stats(const pgc_prefix_cache *cache, pgc_prefix_stats *out);
+/* Entry metadata; tokens_out / pages_out (nullable) receive its token ids and page ids. */
+int pgc_prefix_cache_entry(const pgc_prefix_cache *cache, int64_t index, pgc_prefix_entry *out,
+                           uint32_t *tokens_out, uint64_t tokens_cap, int32_t *pages_out,
+                           int64_t pages_cap);
+/* removeEntry: releases the entry's pages and state slot; later indexes shift down. */
+int pgc_prefix_cache_remove(pgc_prefix_cache *cache, int64_t index);
+/* startDirectEntry (:315-328): an entry with fresh pages for n tokens that the caller prefills
+ * in place; finishDirectEntry (:330-337) records the next token and touches it. */
+int pgc_prefix_cache_start_direct(pgc_prefix_cache *cache, const uint32_t *ids, uint64_t n,
+                                  int pinned, pgc_match *out);
+int pgc_prefix_cache_finish_direct(pgc_prefix_cache *cache, pgc_match match, uint32_t next_token);
+/* setEntryHidden (:258-268): the entry's hidden rows (in its pages) are now real. */
+int pgc_prefix_cache_set_hidden_valid(pgc_prefix_cache *cache, pgc_match match, int valid);
+/* storePrefixFromWork (:344-424): caches ids[0, n) whose rows the work sequence's block table
+ * holds (work_table, >= ceil(n / page_tokens) live pages). reuse (nullable) is the match the
+ * work sequence forked from; that entry is extended in place. suffix_hidden != 0: the work
+ * pages hold real hidden rows for [reuse.len, n). next_token (nullable) caches the next token.
+ * *copy_linear_state (nullable) = 1 when the caller must copy the work sequence's linear state
+ * into the entry's state slot. */
+int pgc_prefix_cache_store(pgc_prefix_cache *cache, const uint32_t *ids, uint64_t n,
+                           const pgc_match *reuse, const int32_t *work_table, int64_t work_pages,
+                           int suffix_hidden, const uint32_t *next_token, int pinned,
+                           pgc_match *out, int *copy_linear_state);
+/* prefixState (:278-283) for paged KV: the first ceil(match.len / page_tokens) pages of the
+ * entry, one reference each taken for the caller, written to table_out. */
+int pgc_prefix_cache_fork(pgc_prefix_cache *cache, pgc_match match, int32_t *table_out,
+                          int64_t table_cap, int64_t *pages_out);
+/* Evicts LRU unpinned entries until `need_free` pages are free (pages still held by running
+ * sequences are not freed by evicting their entry); PGC_ERR_CAPACITY when nothing is left. */
+int pgc_prefix_cache_evict_for_pages(pgc_prefix_cache *cache, int32_t need_free);
+/* loadEntrySlot + finishLoadedEntry (:426-453): clears the cache, then one pinned entry with
+ * fresh pages for a snapshot file's tokens (restore the file image into them), then indexed. */
+int pgc_prefix_cache_load_slot(pgc_prefix_cache *cache, const uint32_t *ids, uint64_t n,
+                               pgc_match *out);
+int pgc_prefix_cache_finish_loaded(pgc_prefix_cache *cache, pgc_match match);
+/* persistedEntryConst (:153-163): the active entry, else the most recently used one. */
+int pgc_prefix_cache_persisted(const pgc_prefix_cache *cache, pgc_match *out);
 
 #ifdef __cplusplus
 }

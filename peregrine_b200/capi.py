@@ -31,8 +31,11 @@ APPEND_PREFILL = 1
 STATUS = {
     0: "PGC_OK", -1: "PGC_ERR_INVALID", -2: "PGC_ERR_BOUNDS", -3: "PGC_ERR_WORKSPACE",
     -4: "PGC_ERR_CUDA", -5: "PGC_ERR_ALIGN", -6: "PGC_ERR_DEVICE", -7: "PGC_ERR_TIMEOUT",
-    -8: "PGC_ERR_CONTEXT", -9: "PGC_ERR_FILE", -10: "PGC_ERR_FORMAT",
+    -8: "PGC_ERR_CONTEXT", -9: "PGC_ERR_FILE", -10: "PGC_ERR_FORMAT", -11: "PGC_ERR_CAPACITY",
 }
+
+
+STATUS_INVALID = -1
 
 
 class PgcError(RuntimeError):
@@ -56,6 +59,30 @@ class PrefixInfo(C.Structure):
     _fields_ = [("token_count", C.c_uint64), ("next_token", C.c_uint32),
                 ("next_token_valid", C.c_uint32), ("hidden_valid", C.c_uint32),
                 ("file_bytes", C.c_uint64)]
+
+
+class Match(C.Structure):
+    _fields_ = [("index", C.c_int64), ("len", C.c_int64)]
+
+    def __eq__(self, other):
+        return isinstance(other, Match) and (self.index, self.len) == (other.index, other.len)
+
+    def __repr__(self):
+        return f"Match(index={self.index}, len={self.len})"
+
+
+class PrefixStats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in (
+        "hits", "misses", "hit_tokens", "computed_tokens", "reserved_tokens", "resident_tokens",
+        "max_tokens", "entry_count", "pinned_count", "evictions", "trie_nodes")] + [
+        ("active_index", C.c_int64)]
+
+
+class PrefixEntry(C.Structure):
+    _fields_ = [("token_count", C.c_uint64), ("page_count", C.c_int64), ("capacity", C.c_uint64),
+                ("state_slot", C.c_int32), ("pinned", C.c_int32), ("hidden_valid", C.c_int32),
+                ("next_token_valid", C.c_int32), ("next_token", C.c_uint32),
+                ("last_access", C.c_uint64), ("hits", C.c_uint64)]
 
 
 P = C.c_void_p
@@ -92,6 +119,38 @@ SIGNATURES = {
     "pgc_prefix_file_read": (I32, [C.c_char_p, U64, U64, U64, P, U64, C.POINTER(PrefixInfo)]),
     "pgc_prefix_file_header": (I32, [P, U64, U64, U64, C.c_uint32, I32, I32]),
     "pgc_prefix_file_write": (I32, [C.c_char_p, P, U64]),
+    "pgc_page_pool_create": (P, [I32]),
+    "pgc_page_pool_destroy": (None, [P]),
+    "pgc_page_pool_alloc": (I32, [P, I32, P]),
+    "pgc_page_pool_retain": (I32, [P, P, I32]),
+    "pgc_page_pool_release": (I32, [P, P, I32]),
+    "pgc_page_pool_refcount": (I32, [P, I32]),
+    "pgc_page_pool_free_pages": (I32, [P]),
+    "pgc_page_pool_make_writable": (I32, [P, P, I32, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    "pgc_prefix_cache_create": (P, [P, I32, U64, U64, I32]),
+    "pgc_prefix_cache_destroy": (None, [P]),
+    "pgc_prefix_cache_clear_all": (None, [P]),
+    "pgc_prefix_cache_enable_hidden_tracking": (None, [P]),
+    "pgc_prefix_cache_find": (I32, [P, P, U64, C.POINTER(Match)]),
+    "pgc_prefix_cache_contains": (I32, [P, P, U64, U64]),
+    "pgc_prefix_cache_touch": (None, [P, Match]),
+    "pgc_prefix_cache_record_hit": (None, [P, U64]),
+    "pgc_prefix_cache_record_miss": (None, [P]),
+    "pgc_prefix_cache_record_computed": (None, [P, U64]),
+    "pgc_prefix_cache_stats": (I32, [P, C.POINTER(PrefixStats)]),
+    "pgc_prefix_cache_entry": (I32, [P, I64, C.POINTER(PrefixEntry), P, U64, P, I64]),
+    "pgc_prefix_cache_remove": (I32, [P, I64]),
+    "pgc_prefix_cache_start_direct": (I32, [P, P, U64, I32, C.POINTER(Match)]),
+    "pgc_prefix_cache_finish_direct": (I32, [P, Match, C.c_uint32]),
+    "pgc_prefix_cache_set_hidden_valid": (I32, [P, Match, I32]),
+    "pgc_prefix_cache_store": (I32, [P, P, U64, C.POINTER(Match), P, I64, I32,
+                                     C.POINTER(C.c_uint32), I32, C.POINTER(Match),
+                                     C.POINTER(C.c_int)]),
+    "pgc_prefix_cache_fork": (I32, [P, Match, P, I64, C.POINTER(C.c_int64)]),
+    "pgc_prefix_cache_evict_for_pages": (I32, [P, I32]),
+    "pgc_prefix_cache_load_slot": (I32, [P, P, U64, C.POINTER(Match)]),
+    "pgc_prefix_cache_finish_loaded": (I32, [P, Match]),
+    "pgc_prefix_cache_persisted": (I32, [P, C.POINTER(Match)]),
 }
 
 _lib = None

@@ -165,6 +165,7 @@ const char *pgc_status_string(int status) {
         case PGC_ERR_CONTEXT: return "invalid context length";
         case PGC_ERR_FILE: return "file missing or not accessible";
         case PGC_ERR_FORMAT: return "prefix-state file failed validation";
+        case PGC_ERR_CAPACITY: return "page pool or state slots exhausted";
         default: return "unknown status";
     }
 }
