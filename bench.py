@@ -288,6 +288,7 @@ def bench_config2(capi, iters=5):
     then a 1600-token chunk: K/V append with RMSNorm + RoPE, causal attention over
     prefix + chunk. The q4 projections are out of scope: the chunk's N(0,1) hidden rows
     [1600x4096] serve directly as Q."""
+    import numpy as np
     import torch
     bf = torch.bfloat16
     g = torch.Generator(device="cuda")
@@ -337,6 +338,33 @@ def bench_config2(capi, iters=5):
         for l in range(layers):
             capi.prefill_attn(q, kp[l], vp[l], table, P, T, SCALE, out, pws, stream=s)
 
+    # The same prefix as a cache hit on the page-refcounted prefix cache: the entry's pages
+    # are forked into the request's block table (host refcounts, KV and hidden rows are not
+    # copied), the partial boundary page (none here: 24576 is page aligned) is copied on write,
+    # and the 24 GD + conv linear states are copied into the request's state, as the
+    # reference's hit path copies them (copyLinearStateFrom).
+    from peregrine_b200 import prefix_cache as pcm
+    ppool = pcm.PagePool(pages)
+    pcache = pcm.PrefixCache(ppool, 65536, T, state_slots=2)
+    ids = np.arange(P, dtype=np.uint32)
+    hit_entry = pcache.start_direct_entry(ids)
+    pcache.finish_direct_entry(hit_entry, 0)
+    hit_pools = kp + vp
+
+    def hit_share():
+        m = pcache.find_prefix(ids)
+        t = pcache.fork(m)
+        if m.len % PAGE:
+            src, dst = ppool.make_writable(t, len(t) - 1)
+            pcm.copy_page(hit_pools, src, dst, stream=s)
+        capi.copy_regions(regions, stream=s)
+        pcache.touch(m)
+        ppool.release(t)
+
+    h_ms = _ev_time(hit_share, iters)
+    hit_bytes = 24 * (32 * 128 * 128 * 4 + 3 * 8192 * 2)
+    pcache.close()
+    ppool.close()
     r_ms = _ev_time(restore, iters)
     a_ms = _ev_time(chunk_append, iters)
     p_ms = _ev_time(prefill, iters)
@@ -347,6 +375,7 @@ def bench_config2(capi, iters=5):
                         "states) from an HBM store, then 1600-token chunk append + causal prefill",
             "restore_ms": round(r_ms, 3), "restore_bytes": restore_bytes,
             "restore_GB_s_read_plus_write": round(2 * restore_bytes / (r_ms * 1e-3) / 1e9, 1),
+            "hit_share_ms": round(h_ms, 3), "hit_share_bytes_copied": hit_bytes,
             "append_ms": round(a_ms, 3), "append_GB_s": round(append_bytes / (a_ms * 1e-3) / 1e9, 1),
             "prefill_ms": round(p_ms, 3), "prefill_flop": flops,
             "prefill_TFLOP_s": round(flops / (p_ms * 1e-3) / 1e12, 1)}

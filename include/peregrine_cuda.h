@@ -392,6 +392,7 @@ typedef struct pgc_prefix_entry {
 } pgc_prefix_entry;
 
 pgc_page_pool *pgc_page_pool_create(int32_t num_pages);
+/* A pool destroyed while caches are built on it is freed with the last of them. */
 void pgc_page_pool_destroy(pgc_page_pool *pool);
 /* n fresh pages with one reference each; PGC_ERR_CAPACITY (nothing taken) when fewer are free. */
 int pgc_page_pool_alloc(pgc_page_pool *pool, int32_t n, int32_t *pages_out);
@@ -407,7 +408,7 @@ int pgc_page_pool_make_writable(pgc_page_pool *pool, int32_t *table, int32_t slo
                                 int32_t *src_page, int32_t *dst_page);
 
 /* Cache.init (prefix_state_cache.zig:312-320) over `pool`, with `state_slots` linear-state
- * slots. The pool must outlive the cache. */
+ * slots. */
 pgc_prefix_cache *pgc_prefix_cache_create(pgc_page_pool *pool, int32_t page_tokens,
                                           uint64_t max_tokens, uint64_t prefill_chunk_tokens,
                                           int32_t state_slots);

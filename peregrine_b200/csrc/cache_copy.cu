@@ -121,6 +121,108 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Vector form of kv_dense_kernel for a 16-byte aligned dense side (dense stride and first
+// token multiples of 8): one CTA per (64-token tile, kv head), no shared-memory staging.
+// Each thread moves one 8x8 block of V (8 value dims x 8 tokens): eight 16-byte loads along
+// the source's contiguous axis, an in-register transpose of 16-bit elements (byte permutes),
+// eight 16-byte stores along the destination's contiguous axis. A warp covers 2 token chunks x
+// 16 dim blocks, so the dense side moves whole 32-byte sectors and the page side 256-byte row
+// halves. K rows are 512 B in both layouts: eight independent 16-byte copies per thread.
+constexpr int kVecTile = 64;
+
+__device__ __forceinline__ void transpose8x8_u16(const uint32_t (&in)[8][4], uint32_t (&out)[8][4]) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+            out[k][m] = __byte_perm(in[2 * m][k >> 1], in[2 * m + 1][k >> 1],
+                                    (k & 1) ? 0x7632u : 0x5410u);
+}
+
+__device__ __forceinline__ void ld4(uint32_t (&r)[4], const uint16_t *p) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(p);
+    r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+}
+
+__device__ __forceinline__ void st4(uint16_t *p, const uint32_t (&r)[4]) {
+    *reinterpret_cast<uint4 *>(p) = make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+__global__ void __launch_bounds__(256)
+    kv_dense_vec_kernel(bool restore, uint16_t *dk, uint16_t *dv, int64_t dstride, int64_t dtok,
+                        uint16_t *kp, uint16_t *vp, int64_t num_pages, const int32_t *table,
+                        int64_t n_table, int64_t ptok, int64_t count) {
+    __shared__ int64_t rows[kVecTile];
+    const int kvh = blockIdx.y;
+    const int64_t base = (int64_t)blockIdx.x * kVecTile;
+    const int n = (int)(count - base < kVecTile ? count - base : kVecTile);
+    const int tid = threadIdx.x;
+    if (tid < kVecTile) rows[tid] = tid < n ? paged_row(table, n_table, num_pages, ptok + base + tid, kvh) : -1;
+    __syncthreads();
+
+    // K: 64 tokens x 32 uint4, loads first for memory-level parallelism
+    {
+        uint4 buf[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = tid + j * 256, tt = i >> 5, u = i & 31;
+            if (tt < n && rows[tt] >= 0) {
+                const uint4 *src = restore
+                    ? reinterpret_cast<const uint4 *>(dk + ((int64_t)kvh * dstride + dtok + base + tt) * kHeadDim) + u
+                    : reinterpret_cast<const uint4 *>(kp + rows[tt]) + u;
+                buf[j] = *src;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = tid + j * 256, tt = i >> 5, u = i & 31;
+            if (tt < n && rows[tt] >= 0) {
+                uint4 *dst = restore
+                    ? reinterpret_cast<uint4 *>(kp + rows[tt]) + u
+                    : reinterpret_cast<uint4 *>(dk + ((int64_t)kvh * dstride + dtok + base + tt) * kHeadDim) + u;
+                *dst = buf[j];
+            }
+        }
+    }
+
+    // V: one 8x8 block per thread
+    const int w = tid >> 5, l = tid & 31;
+    const int d0 = ((l & 15) + 16 * (w >> 2)) * 8;
+    const int t0 = (2 * (w & 3) + (l >> 4)) * 8;
+    if (t0 >= n) return;
+    bool full = t0 + 8 <= n;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) full = full && rows[t0 + k] >= 0;
+    uint16_t *dcol = dv + ((int64_t)kvh * kHeadDim + d0) * dstride + dtok + base + t0;
+    if (full) {
+        uint32_t a[8][4], b[8][4];
+        if (restore) {
+#pragma unroll
+            for (int r = 0; r < 8; ++r) ld4(a[r], dcol + (int64_t)r * dstride);
+            transpose8x8_u16(a, b);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) st4(vp + rows[t0 + k] + d0, b[k]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) ld4(a[k], vp + rows[t0 + k] + d0);
+            transpose8x8_u16(a, b);
+#pragma unroll
+            for (int r = 0; r < 8; ++r) st4(dcol + (int64_t)r * dstride, b[r]);
+        }
+        return;
+    }
+    // ragged tail chunk (or a token whose row failed to resolve): element by element
+    const int m = n - t0 < 8 ? n - t0 : 8;
+    for (int k = 0; k < m; ++k) {
+        const int64_t pr = rows[t0 + k];
+        if (pr < 0) continue;
+        for (int r = 0; r < 8; ++r) {
+            if (restore) vp[pr + d0 + r] = dcol[(int64_t)r * dstride + k];
+            else dcol[(int64_t)r * dstride + k] = vp[pr + d0 + r];
+        }
+    }
+}
+
 // paged -> paged, one warp per (token, kv head): 512 B of K and 512 B of V
 __global__ void __launch_bounds__(256)
     kv_copy_tokens_kernel(const uint16_t *sk, const uint16_t *sv, int64_t s_pages,
@@ -214,7 +316,13 @@ cudaError_t launch_kv_dense(bool restore, uint16_t *dense_k, uint16_t *dense_v,
     if (count == 0) return cudaSuccess;
     dim3 grid((unsigned)((count + kDenseTile - 1) / kDenseTile), kNumKvHeads);
     const uintptr_t a = reinterpret_cast<uintptr_t>(dense_k);
-    if (a % 16 == 0)
+    const uintptr_t av = reinterpret_cast<uintptr_t>(dense_v);
+    if (a % 16 == 0 && av % 16 == 0 && dense_stride % 8 == 0 && dense_token % 8 == 0) {
+        dim3 vgrid((unsigned)((count + kVecTile - 1) / kVecTile), kNumKvHeads);
+        kv_dense_vec_kernel<<<vgrid, 256, 0, stream>>>(restore, dense_k, dense_v, dense_stride,
+                                                       dense_token, k_pages, v_pages, num_pages,
+                                                       table, n_table, page_token, count);
+    } else if (a % 16 == 0)
         kv_dense_kernel<uint4><<<grid, 256, 0, stream>>>(restore, dense_k, dense_v, dense_stride,
                                                          dense_token, k_pages, v_pages, num_pages,
                                                          table, n_table, page_token, count);

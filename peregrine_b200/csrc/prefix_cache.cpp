@@ -30,6 +30,8 @@
 struct pgc_page_pool {
     std::vector<int32_t> ref;        // refcount per page (0 = free)
     std::vector<int32_t> free_list;  // stack of free page ids, lowest id on top
+    int attached = 0;                // caches built on this pool
+    bool destroy_requested = false;  // destroyed while caches were attached: freed with the last
 };
 
 namespace {
@@ -60,10 +62,15 @@ void pool_release(pgc_page_pool *p, const int32_t *pages, int64_t n) {
         if (--p->ref[pages[i]] == 0) p->free_list.push_back(pages[i]);
 }
 
-// ---------------------------------------------------------------------------- token trie
-// Same contract as the reference index (prefix_state_cache.zig:21-213): one node per token,
-// a node may carry an entry index, removing an entry prunes nodes that carry nothing.
-// Children are found through one hash map keyed by (parent, token) instead of per-node lists.
+// ---------------------------------------------------------------------------- prefix index
+// Same contract as the reference index (prefix_state_cache.zig:21-213) — insert a token
+// sequence with an entry index, exact and longest-prefix lookup, removal that prunes nodes
+// carrying nothing — but path-compressed: a node holds the run of tokens on the edge from its
+// parent, so a lookup compares token spans instead of one hash probe per token (a 24k-token
+// prompt walks a handful of nodes). Nodes keep their id while the tree is re-shaped (a split
+// inserts the new node above; a merge folds the parent into its only child), so an entry can
+// remember the id of the node it ends at. Children are found through one hash map keyed by
+// (node, first token of the child's run).
 class Trie {
   public:
     void clear() {
@@ -72,21 +79,31 @@ class Trie {
         child_.clear();
     }
 
-    // Node for `tokens` (creating the path); the node's entry is set to `entry`.
+    // Node ending exactly at `tokens` (splitting an edge or adding a leaf as needed), whose
+    // entry is set to `entry`.
     int32_t insert(const uint32_t *tokens, uint64_t n, int64_t entry) {
         ensure_root();
         int32_t node = 0;
-        for (uint64_t i = 0; i < n; ++i) {
-            const uint64_t key = edge(node, tokens[i]);
-            auto it = child_.find(key);
-            if (it != child_.end()) {
-                node = it->second;
-                continue;
+        uint64_t i = 0;
+        while (i < n) {
+            auto it = child_.find(edge(node, tokens[i]));
+            if (it == child_.end()) {
+                const int32_t leaf = alloc(node, tokens + i, n - i);
+                child_.emplace(edge(node, tokens[i]), leaf);
+                ++nodes_[node].children;
+                node = leaf;
+                i = n;
+                break;
             }
-            const int32_t c = alloc(node, tokens[i]);
-            child_.emplace(key, c);
-            ++nodes_[node].children;
-            node = c;
+            const int32_t c = it->second;
+            const uint64_t l = common(nodes_[c].run, tokens + i, n - i);
+            if (l < nodes_[c].run.size()) {
+                split(c, l);
+                node = nodes_[c].parent;  // the new node ending after l tokens
+            } else {
+                node = c;
+            }
+            i += l;
         }
         nodes_[node].entry = entry;
         return node;
@@ -95,10 +112,14 @@ class Trie {
     int32_t find_node(const uint32_t *tokens, uint64_t n) const {
         if (nodes_.empty()) return -1;
         int32_t node = 0;
-        for (uint64_t i = 0; i < n; ++i) {
+        uint64_t i = 0;
+        while (i < n) {
             auto it = child_.find(edge(node, tokens[i]));
             if (it == child_.end()) return -1;
+            const Node &c = nodes_[it->second];
+            if (c.run.size() > n - i || common(c.run, tokens + i, n - i) != c.run.size()) return -1;
             node = it->second;
+            i += c.run.size();
         }
         return node;
     }
@@ -114,14 +135,18 @@ class Trie {
     bool find_longest(const uint32_t *prompt, uint64_t n, int64_t *entry, uint64_t *len) const {
         if (nodes_.empty()) return false;
         int32_t node = 0;
+        uint64_t i = 0;
         bool found = false;
-        for (uint64_t i = 0; i < n; ++i) {
+        while (i < n) {
             auto it = child_.find(edge(node, prompt[i]));
             if (it == child_.end()) break;
+            const Node &c = nodes_[it->second];
+            if (c.run.size() > n - i || common(c.run, prompt + i, n - i) != c.run.size()) break;
             node = it->second;
-            if (nodes_[node].entry >= 0) {
-                *entry = nodes_[node].entry;
-                *len = i + 1;
+            i += c.run.size();
+            if (c.entry >= 0) {
+                *entry = c.entry;
+                *len = i;
                 found = true;
             }
         }
@@ -135,44 +160,98 @@ class Trie {
   private:
     struct Node {
         int32_t parent = -1;
-        uint32_t token = 0;
         int32_t children = 0;
         int64_t entry = -1;
+        std::vector<uint32_t> run;  // tokens on the edge from the parent
     };
 
     static uint64_t edge(int32_t parent, uint32_t token) {
         return ((uint64_t)(uint32_t)parent << 32) | token;
     }
 
+    static uint64_t common(const std::vector<uint32_t> &run, const uint32_t *t, uint64_t n) {
+        const uint64_t m = std::min<uint64_t>(run.size(), n);
+        // whole runs usually match: compare 1024-token blocks with memcmp, then finish the
+        // first differing block token by token
+        uint64_t i = 0;
+        while (i + 1024 <= m && std::memcmp(run.data() + i, t + i, 1024 * 4) == 0) i += 1024;
+        while (i < m && run[i] == t[i]) ++i;
+        return i;
+    }
+
     void ensure_root() {
         if (nodes_.empty()) nodes_.push_back(Node{});
     }
 
-    int32_t alloc(int32_t parent, uint32_t token) {
+    int32_t alloc(int32_t parent, const uint32_t *run, uint64_t len) {
         Node nd;
         nd.parent = parent;
-        nd.token = token;
+        nd.run.assign(run, run + len);
         if (!free_.empty()) {
             const int32_t i = free_.back();
             free_.pop_back();
-            nodes_[i] = nd;
+            nodes_[i] = std::move(nd);
             return i;
         }
-        nodes_.push_back(nd);
+        nodes_.push_back(std::move(nd));
         return (int32_t)nodes_.size() - 1;
     }
 
+    // New node above c holding the first l tokens of c's run; c keeps its id.
+    void split(int32_t c, uint64_t l) {
+        const int32_t parent = nodes_[c].parent;
+        const uint32_t first = nodes_[c].run[0];
+        const int32_t mid = alloc(parent, nodes_[c].run.data(), l);  // may move nodes_
+        Node &cn = nodes_[c];
+        cn.run.erase(cn.run.begin(), cn.run.begin() + (int64_t)l);
+        cn.parent = mid;
+        nodes_[mid].children = 1;
+        child_[edge(parent, first)] = mid;
+        child_.emplace(edge(mid, cn.run[0]), c);
+    }
+
+    void unlink(int32_t node) {
+        Node &nd = nodes_[node];
+        child_.erase(edge(nd.parent, nd.run[0]));
+        --nodes_[nd.parent].children;
+        nodes_[node] = Node{};
+        free_.push_back(node);
+    }
+
+    // After node lost its entry: drop it if it is a leaf, fold it into its only child if it
+    // has one, then do the same for a parent left without entry and with at most one child.
     void prune(int32_t node) {
         while (node != 0) {
             Node &nd = nodes_[node];
-            if (nd.entry >= 0 || nd.children != 0) return;
+            if (nd.entry >= 0 || nd.children > 1) return;
             const int32_t parent = nd.parent;
-            child_.erase(edge(parent, nd.token));
-            --nodes_[parent].children;
-            nd = Node{};
-            free_.push_back(node);
-            node = parent;
+            if (nd.children == 0) {
+                unlink(node);
+                node = parent;
+                continue;
+            }
+            // one child: the child absorbs this node's run and takes its place under parent
+            int32_t only = -1;
+            for (const auto &kv : child_)
+                if ((int32_t)(kv.first >> 32) == node) {
+                    only = kv.second;
+                    break;
+                }
+            fold_into_child(node, only);
+            return;
         }
+    }
+
+    void fold_into_child(int32_t node, int32_t only) {
+        Node &nd = nodes_[node];
+        Node &ch = nodes_[only];
+        const int32_t parent = nd.parent;
+        child_.erase(edge(node, ch.run[0]));
+        child_[edge(parent, nd.run[0])] = only;
+        ch.run.insert(ch.run.begin(), nd.run.begin(), nd.run.end());
+        ch.parent = parent;
+        nodes_[node] = Node{};
+        free_.push_back(node);
     }
 
     std::vector<Node> nodes_;
@@ -385,7 +464,11 @@ pgc_page_pool *pgc_page_pool_create(int32_t num_pages) {
     return p;
 }
 
-void pgc_page_pool_destroy(pgc_page_pool *pool) { delete pool; }
+void pgc_page_pool_destroy(pgc_page_pool *pool) {
+    if (!pool) return;
+    if (pool->attached > 0) pool->destroy_requested = true;  // the last cache frees it
+    else delete pool;
+}
 
 int pgc_page_pool_alloc(pgc_page_pool *pool, int32_t n, int32_t *pages_out) {
     if (!pool || n < 0 || (n > 0 && !pages_out)) return PGC_ERR_INVALID;
@@ -401,13 +484,22 @@ int pgc_page_pool_retain(pgc_page_pool *pool, const int32_t *pages, int32_t n) {
 
 int pgc_page_pool_release(pgc_page_pool *pool, const int32_t *pages, int32_t n) {
     if (!pool || n < 0 || (n > 0 && !pages)) return PGC_ERR_INVALID;
-    // a page listed twice must hold two references
-    std::unordered_map<int32_t, int32_t> count;
+    if (!pages_live(pool, pages, n)) return PGC_ERR_BOUNDS;
+    // a page listed twice must hold two references: drop them all, and undo everything if
+    // one went below zero
     for (int32_t i = 0; i < n; ++i) {
-        if (!pages_live(pool, pages + i, 1)) return PGC_ERR_BOUNDS;
-        if (++count[pages[i]] > pool->ref[pages[i]]) return PGC_ERR_BOUNDS;
+        if (--pool->ref[pages[i]] < 0) {
+            for (int32_t j = 0; j <= i; ++j) ++pool->ref[pages[j]];
+            return PGC_ERR_BOUNDS;
+        }
     }
-    pool_release(pool, pages, n);
+    for (int32_t i = 0; i < n; ++i)
+        if (pool->ref[pages[i]] == 0) {
+            pool->free_list.push_back(pages[i]);
+            pool->ref[pages[i]] = -1;  // listed again below: push once
+        }
+    for (int32_t i = 0; i < n; ++i)
+        if (pool->ref[pages[i]] < 0) pool->ref[pages[i]] = 0;
     return PGC_OK;
 }
 
@@ -448,6 +540,7 @@ pgc_prefix_cache *pgc_prefix_cache_create(pgc_page_pool *pool, int32_t page_toke
     pgc_prefix_cache *c = new (std::nothrow) pgc_prefix_cache;
     if (!c) return nullptr;
     c->pool = pool;
+    ++pool->attached;
     c->page_tokens = page_tokens;
     c->max_tokens = max_tokens;
     c->initial_state_tokens = std::min(max_tokens, prefill_chunk_tokens);
@@ -459,7 +552,9 @@ pgc_prefix_cache *pgc_prefix_cache_create(pgc_page_pool *pool, int32_t page_toke
 void pgc_prefix_cache_destroy(pgc_prefix_cache *cache) {
     if (!cache) return;
     cache->clear_all();
+    pgc_page_pool *pool = cache->pool;
     delete cache;
+    if (--pool->attached == 0 && pool->destroy_requested) delete pool;
 }
 
 void pgc_prefix_cache_clear_all(pgc_prefix_cache *cache) {

@@ -95,7 +95,14 @@ def test_copy_rows_from_pinned_host_store(cuda):
     assert torch.equal(pool.cpu()[table.long()], store)
 
 
-def test_dense_restore_snapshot_bit_exact(cuda, oracle):
+# (restore dense token, page token, count, snapshot dense token, snapshot count): the first case
+# takes the element-wise kernel (dense token not a multiple of 8), the others the vector kernel
+# with ragged 64-token tiles and 8-token chunks
+@pytest.mark.parametrize("src_tok,dst_tok,count,snap_tok,snap_count",
+                         [(100, 21, 777, 3, 900), (96, 21, 777, 8, 901), (0, 0, 1000, 0, 1000),
+                          (8, 5, 7, 16, 63)])
+def test_dense_restore_snapshot_bit_exact(cuda, oracle, src_tok, dst_tok, count, snap_tok,
+                                          snap_count):
     import torch
     rng = np.random.default_rng(2)
     stride = oracle.full_cache_stride_for_max_seq(1000)
@@ -106,7 +113,6 @@ def test_dense_restore_snapshot_bit_exact(cuda, oracle):
     kp = rng.integers(0, 65535, (npages, NKV, PAGE, D), dtype=np.uint16)
     vp = rng.integers(0, 65535, (npages, NKV, PAGE, D), dtype=np.uint16)
     kpd, vpd = dev(kp), dev(vp)
-    count, src_tok, dst_tok = 777, 100, 21
     cuda.kv_restore_dense(dev(kd), dev(vd), stride, src_tok, kpd, vpd, dev(table), dst_tok, count)
     assert oracle.kv_restore_dense(kd, vd, stride, src_tok, kp, vp, table, dst_tok, count) == 0
     torch.cuda.synchronize()
@@ -114,8 +120,8 @@ def test_dense_restore_snapshot_bit_exact(cuda, oracle):
     k2 = np.zeros_like(kd)
     v2 = np.zeros_like(vd)
     k2d, v2d = dev(k2), dev(v2)
-    cuda.kv_snapshot_dense(kpd, vpd, dev(table), 5, k2d, v2d, stride, 3, 900)
-    assert oracle.kv_snapshot_dense(kp, vp, table, 5, k2, v2, stride, 3, 900) == 0
+    cuda.kv_snapshot_dense(kpd, vpd, dev(table), 5, k2d, v2d, stride, snap_tok, snap_count)
+    assert oracle.kv_snapshot_dense(kp, vp, table, 5, k2, v2, stride, snap_tok, snap_count) == 0
     torch.cuda.synchronize()
     assert np.array_equal(host_u16(k2d), k2) and np.array_equal(host_u16(v2d), v2)
 

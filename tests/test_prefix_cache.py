@@ -256,12 +256,13 @@ def test_start_direct_and_load_slot_evict_for_pages(pc):
     assert c.persisted_entry() == m and c.pinned_entry_count() == 1
 
 
-def test_random_walk_keeps_bookkeeping_consistent(pc):
+@pytest.mark.parametrize("seed", [5, 6, 7])
+def test_random_walk_keeps_bookkeeping_consistent(pc, seed):
     """Seeded random operations; after each: every page's refcount equals its holders (entries
     + live sequences), free pages complement the held ones, reserved tokens equal the sum of
     entry capacities and stay within the budget, and every entry is found by its own tokens."""
     from peregrine_b200.capi import PgcError
-    rng = np.random.default_rng(5)
+    rng = np.random.default_rng(seed)
     npages = 96
     pool, c = _cache(pc, 600, 48, pages=npages, slots=6)
     bases = [list(rng.integers(0, 50, 100)) for _ in range(3)]
@@ -316,6 +317,39 @@ def test_random_walk_keeps_bookkeeping_consistent(pc):
         assert pool.free_pages == int((refs == 0).sum())
         assert s.reserved_tokens == cap <= 600
     assert stores > 100 and reuses > 50 and c.stats().evictions > 20
+    # the path-compressed index holds at most two nodes per entry, and only the root when empty
+    assert c.stats().trie_nodes <= 2 * c.entry_count() + 1
+    for i in reversed(range(c.entry_count())):
+        c.remove_entry(i)
+    assert c.stats().trie_nodes == 1
+    for t in seqs:
+        pool.release(t)
+    assert pool.free_pages == npages
+
+
+def test_index_splits_and_folds_runs(pc):
+    """Split an edge (a shorter prefix, a branch), then remove entries so that nodes fold back;
+    every remaining entry is still found with its own length."""
+    _, c = _cache(pc, 10_000, 16)
+    long_ = list(range(100))
+    _add(c, long_, False, 1)
+    assert c.stats().trie_nodes == 2
+    _add(c, long_[:50], False, 2)        # split at 50
+    _add(c, long_[:50] + [7, 7], False, 3)  # branch at 50
+    _add(c, long_[:25], False, 4)        # split at 25
+    assert c.stats().trie_nodes == 5
+    assert c.find_prefix(long_ + [1]).len == 100
+    assert c.find_prefix(long_[:60]).len == 50
+    assert c.find_prefix(long_[:50] + [7, 7, 7]).len == 52
+    assert c.find_prefix(long_[:30]).len == 25
+    assert c.find_prefix(long_[:24]) is None
+    c.remove_entry(c.find_prefix(long_[:50]).index)  # node at 50 keeps two children
+    assert c.stats().trie_nodes == 5 and c.find_prefix(long_[:60]).len == 25
+    c.remove_entry(c.find_prefix(long_[:50] + [7, 7]).index)  # 50 folds into the long leaf
+    assert c.stats().trie_nodes == 3
+    assert c.find_prefix(long_ + [1]).len == 100 and c.find_prefix(long_[:60]).len == 25
+    c.remove_entry(c.find_prefix(long_[:30]).index)  # 25 folds too
+    assert c.stats().trie_nodes == 2 and c.find_prefix(long_).len == 100
 
 
 # ------------------------------------------------------------------------------------- GPU
