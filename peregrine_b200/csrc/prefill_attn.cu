@@ -14,9 +14,9 @@
 // (row r = token r/4, head r%4), so the pair's MMAs have M = 256 and every K/V tile serves 64
 // tokens x 4 heads. The leader CTA issues S = Q K^T (M256 N128 K256) and O += P V (M256 N256
 // K128) for both; each CTA stages its own Q, 64 of the tile's 128 keys and 128 of the 256 value
-// dims, so each SM fetches half of every K/V tile. Per CTA (352 threads): warps 0-7 softmax +
-// epilogue (two warps per TMEM lane quarter, splitting key columns and O dims), warp 8 the MMA
-// issuer (leader only), warp 9 the Q/K TMA producer, warp 10 the V producer. TMEM: O in columns
+// dims, so each SM fetches half of every K/V tile. Per CTA (672 threads): warps 0-15 softmax +
+// epilogue (four warps per TMEM lane quarter, splitting key columns and O dims), warp 16 the MMA
+// issuer (leader only), warps 17-18 the Q/K TMA producers, warps 19-20 the V producers. TMEM: O in columns
 // [0,256), two S tiles in [256,512); P(j) is written over the first 64 columns of S(j).
 #include <cuda.h>
 
@@ -288,7 +288,12 @@ __device__ __forceinline__ bool wait_or_abort_cluster(uint64_t *bar, uint32_t pa
 // =============================================================================================
 namespace pair {
 
-constexpr int kThreads = 352;         // warps 0-7 softmax, 8 MMA, 9 K (+Q) TMA, 10 V TMA
+constexpr int kSoftmaxWarps = 16;
+// warps 0-15 softmax, 16 MMA, 17-18 K (+Q) TMA, 19-20 V TMA. TMA boxes here are one page high
+// (2 KiB); an SM retires them roughly twice as fast when two warps issue in parallel, so each
+// operand has two producer warps.
+constexpr int kProducerWarps = 2;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 1 + 2 * kProducerWarps);
 constexpr int kBNp = 128;             // keys per tile
 constexpr int kQBytesP = kBM * kHeadDim * 2;      // [4 dim blocks][128 rows][128 B] = 64 KiB
 constexpr int kKHalf = 64 * kHeadDim * 2;         // this CTA's 64 keys: [4][64][128 B] = 32 KiB
@@ -307,7 +312,7 @@ struct Smem2 {
     // v_empty[2], s_full[2], pv_done[2]
     static constexpr int kNumBars = 1 + kKSlotsP + kVSlotsP + 2 + kKSlotsP + kVSlotsP + 2 + 2;
     static constexpr int kRed = kBar + kNumBars * 8;
-    static constexpr int kTmemSlot = kRed + 2 * 2 * kBM * 4;
+    static constexpr int kTmemSlot = kRed + 4 * kBM * 4;  // red: [4 key quarters][128 rows] fp32
     static constexpr int kAbort = kTmemSlot + 8;
     static constexpr int kBytes = kTmemSlot + 16;
 };
@@ -344,7 +349,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
     uint64_t *q_full = bars;                       // leader: both CTAs' Q bytes
     uint64_t *k_full = q_full + 1;                 // leader [3]: both CTAs' K halves
     uint64_t *v_full = k_full + kKSlotsP;          // leader [2]: both CTAs' V halves
-    uint64_t *p_full = v_full + kVSlotsP;          // leader [2]: 16 softmax-warp arrivals
+    uint64_t *p_full = v_full + kVSlotsP;          // leader [2]: both CTAs' softmax warps
     uint64_t *k_empty = p_full + 2;                // each [3]
     uint64_t *v_empty = k_empty + kKSlotsP;        // each [2]
     uint64_t *s_full = v_empty + kVSlotsP;         // each [2]
@@ -358,15 +363,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
         *abort_flag = 0;
         mbar_init(q_full, 2);
         for (int s = 0; s < kKSlotsP; ++s) {
-            mbar_init(&k_full[s], 2);
+            mbar_init(&k_full[s], 2 * kProducerWarps);  // leader: both CTAs' K producers
             mbar_init(&k_empty[s], 1);
         }
         for (int s = 0; s < kVSlotsP; ++s) {
-            mbar_init(&v_full[s], 2);  // leader: both CTAs' V halves
+            mbar_init(&v_full[s], 2 * kProducerWarps);  // leader: both CTAs' V producers
             mbar_init(&v_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&p_full[b], 16);
+            mbar_init(&p_full[b], 2 * kSoftmaxWarps);
             mbar_init(&s_full[b], 1);
             mbar_init(&pv_done[b], 1);
         }
@@ -385,16 +390,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
     if (threadIdx.x == 0) PF_DIAG(0, 100 + (int)rank);
     auto leader_addr = [&](uint64_t *bar) { return cluster_map(smem_u32(bar), 0); };
 
-    if (warp == 9) {
+    if (warp >= kSoftmaxWarps + 1 && warp < kSoftmaxWarps + 1 + kProducerWarps) {
         // ------------------------------------------------------------ TMA: Q and this CTA's K half
+        // producer kw loads pages {2kw, 2kw+1} of this CTA's 64 keys (4 boxes of 64 dims each)
+        const int kw = warp - (kSoftmaxWarps + 1);
         if (lane == 0) {
-            tma_prefetch_desc(&tmq);
-            tma_prefetch_desc(&tmk);
             const uint64_t pol = l2_policy_evict_last();
-            const uint32_t qbar = leader_addr(q_full);
-            mbar_arrive_expect_tx_cluster(qbar, kQBytesP);
-            for (int c = 0; c < 4; ++c)
-                tma_load_3d_pair(smem + Smem2::kQ + c * (kBM * 128), &tmq, c * 64, kvh * kGroup, tok0, qbar);
+            if (kw == 0) {
+                tma_prefetch_desc(&tmq);
+                tma_prefetch_desc(&tmk);
+                const uint32_t qbar = leader_addr(q_full);
+                mbar_arrive_expect_tx_cluster(qbar, kQBytesP);
+                for (int c = 0; c < 4; ++c)
+                    tma_load_3d_pair(smem + Smem2::kQ + c * (kBM * 128), &tmq, c * 64, kvh * kGroup, tok0, qbar);
+            }
             for (int j = 0; j < n_loc; ++j) {
                 const int sl = j % kKSlotsP;
                 if (j >= kKSlotsP &&
@@ -402,12 +411,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                     break;
                 const int key0 = (tb + j) * kBNp + (int)rank * 64;  // this CTA's 64 keys
                 int npg = 0;
-                for (int pp = 0; pp < 4; ++pp)
+                for (int pp = 2 * kw; pp < 2 * kw + 2; ++pp)
                     if (key0 + pp * kPage < total_keys) ++npg;
                 const uint32_t kbar = leader_addr(&k_full[sl]);
                 mbar_arrive_expect_tx_cluster(kbar, (uint32_t)npg * 4 * 2048);
                 uint8_t *dst = smem + Smem2::kK + sl * kKHalf;
-                for (int pp = 0; pp < npg; ++pp) {
+                for (int pp = 2 * kw; pp < 2 * kw + npg; ++pp) {
                     int page = p.block_table[(key0 >> 4) + pp];
                     if (page < 0 || page >= p.num_pages) {
                         record_error(&g_prefill_err, kErrPageOutOfRange, page);
@@ -420,14 +429,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                 }
             }
         }
-    } else if (warp == 10) {
+    } else if (warp >= kSoftmaxWarps + 1 + kProducerWarps) {
         // ------------------------------------------------------------ TMA: this CTA's V half
         // (value dims [128 * rank, +128) of all 128 keys), counted on the leader's barrier like
-        // K. Rows past the cache end are zeroed here and a partial final page is copied row by
-        // row by the whole warp, so no stale slot (possibly a NaN pattern) meets a zero
-        // probability in P.V, and the softmax warps never wait on V.
+        // K. Producer vw owns keys [64 vw, +64) (pages 4vw..4vw+3). Rows past the cache end are
+        // zeroed here and a partial final page is copied row by row by the whole warp, so no
+        // stale slot (possibly a NaN pattern) meets a zero probability in P.V, and the softmax
+        // warps never wait on V.
+        const int vw = warp - (kSoftmaxWarps + 1 + kProducerWarps);
+        const int r0 = vw * 64, r1 = r0 + 64;  // this producer's key rows of the tile
         {
-            if (lane == 0) tma_prefetch_desc(&tmv);
+            if (lane == 0 && vw == 0) tma_prefetch_desc(&tmv);
             const uint64_t pol = l2_policy_evict_last();
             for (int j = 0; j < n_loc; ++j) {
                 const int sl = j % kVSlotsP;
@@ -439,18 +451,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                 const int valid = min(kBNp, total_keys - key0);  // keys of this tile in the cache
                 const int full_pages = valid / kPage;            // loaded by TMA
                 uint8_t *dst = smem + Smem2::kV + sl * kVHalf;
-                if (valid < kBNp) {
-                    // rows [full_pages*16, 128): zero, then copy the partial page's valid rows
-                    const int first = full_pages * kPage;
-                    for (int i = lane; i < (kBNp - first) * 2 * 8; i += 32) {
+                const int first = max(full_pages * kPage, r0);   // first row not loaded by TMA
+                if (first < r1) {
+                    // rows [first, r1): zero, then copy the partial page's valid rows
+                    for (int i = lane; i < (r1 - first) * 2 * 8; i += 32) {
                         const int row = first + i / 16;
                         const int u = i % 16;
                         *reinterpret_cast<uint4 *>(dst + (u >> 3) * (kBNp * 128) + row * 128 + (u & 7) * 16) =
                             make_uint4(0, 0, 0, 0);
                     }
                     __syncwarp();
-                    const int tail = valid - first;  // valid rows in the partial page (0..15)
-                    if (tail > 0) {
+                    const int tail = valid - full_pages * kPage;  // valid rows in the partial page
+                    if (tail > 0 && full_pages * kPage >= r0 && full_pages * kPage < r1) {
                         int page = p.block_table[(key0 >> 4) + full_pages];
                         if (page < 0 || page >= p.num_pages) {
                             if (lane == 0) record_error(&g_prefill_err, kErrPageOutOfRange, page);
@@ -462,7 +474,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                             const int db = u >> 3, unit = u & 7;
                             const uint4 v = *reinterpret_cast<const uint4 *>(
                                 src + (int64_t)rr * kHeadDim + ((int)rank * 2 + db) * 64 + unit * 8);
-                            const int row = first + rr;
+                            const int row = full_pages * kPage + rr;
                             *reinterpret_cast<uint4 *>(dst + db * (kBNp * 128) + row * 128 +
                                                        ((unit ^ (row & 7)) << 4)) = v;
                         }
@@ -471,10 +483,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                     __syncwarp();
                 }
                 if (lane == 0) {
+                    const int pp0 = r0 / kPage, pp1 = min(full_pages, r1 / kPage);
                     const uint32_t vbar = leader_addr(&v_full[sl]);
-                    mbar_arrive_expect_tx_cluster(vbar, (uint32_t)full_pages * 2 * 2048);
+                    mbar_arrive_expect_tx_cluster(vbar, (uint32_t)max(pp1 - pp0, 0) * 2 * 2048);
                     PF_DIAG(7, j + 1);
-                    for (int pp = 0; pp < full_pages; ++pp) {
+                    for (int pp = pp0; pp < pp1; ++pp) {
                         int page = p.block_table[(key0 >> 4) + pp];
                         if (page < 0 || page >= p.num_pages) {
                             record_error(&g_prefill_err, kErrPageOutOfRange, page);
@@ -490,7 +503,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                 __syncwarp();
             }
         }
-    } else if (warp == 8) {
+    } else if (warp == kSoftmaxWarps) {
         // ------------------------------------------------------------ pair MMA issuer (leader)
         if (leader && lane == 0) {
             constexpr uint32_t idesc_s = umma_idesc(2 * kBM, kBNp, false, false);
@@ -543,10 +556,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ softmax + epilogue
-        // Warps w and w+4 share TMEM lanes 32*(w%4)..+31 (one accumulator row per thread) and
-        // split each 128-key S tile into key halves [64*h, +64) and O into dims [128*h, +128).
+        // Warps w, w+4, w+8 and w+12 share TMEM lanes 32*(w%4)..+31 (one accumulator row per
+        // thread) and split each 128-key S tile into key quarters [32*cg, +32) and O into dims
+        // [64*cg, +64). Four warps per lane quarter keep four independent load -> max -> exp2 ->
+        // store chains in flight on every SM sub-partition. The row maximum is taken on the raw
+        // scores and the 1/16 * log2(e) scale is folded into the exp2 argument (one FMA).
         const int qd = warp & 3;
-        const int h = warp >> 2;
+        const int cg = warp >> 2;
         const int r = qd * 32 + lane;
         const int t = tok0 + r / kGroup;
         const int g = r % kGroup;
@@ -554,48 +570,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
         const int vis = P + t;
         const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
         const int64_t orow = (int64_t)t * kNumQHeads + kvh * kGroup + g;
-        float *red = reinterpret_cast<float *>(smem + Smem2::kRed);
+        float *red = reinterpret_cast<float *>(smem + Smem2::kRed);  // [4 key quarters][128 rows]
         const uint32_t pbar[2] = {leader_addr(&p_full[0]), leader_addr(&p_full[1])};
+        const float c = p.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < n_loc; ++j) {
             const int b = j & 1;
             if (!wait_or_abort(&s_full[b], (j >> 1) & 1, abort_flag, 6)) { ok = false; break; }
             tc_fence_after();
-            float sv[64];
-            {
-                float a[32], c2[32];
-                if (threadIdx.x == 0) PF_DIAG(4, j + 1);
-                if (threadIdx.x == 0) PF_TRACE(3, j);
-                tmem_ld32(tmem + lane_addr + kTS + b * kBNp + h * 64, a);
-                tmem_ld32(tmem + lane_addr + kTS + b * kBNp + h * 64 + 32, c2);
-                tmem_wait_ld();
-                if (threadIdx.x == 0) PF_TRACE(5, j);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) { sv[i] = a[i]; sv[32 + i] = c2[i]; }
-            }
-            const int tile0 = (tb + j) * kBNp;
-            const int key0 = tile0 + h * 64;
+            if (threadIdx.x == 0) PF_DIAG(4, j + 1);
+            if (threadIdx.x == 0) PF_TRACE(3, j);
+            float sv[32];
+            tmem_ld32(tmem + lane_addr + kTS + b * kBNp + cg * 32, sv);
+            tmem_wait_ld();
+            if (threadIdx.x == 0) PF_TRACE(5, j);
+            const int key0 = (tb + j) * kBNp + cg * 32;
             float mx = -INFINITY;
-            if (key0 + 63 <= vis && row_ok) {
+            if (key0 + 31 <= vis && row_ok) {
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    sv[i] *= p.scale_log2;
-                    mx = fmaxf(mx, sv[i]);
-                }
+                for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
             } else {
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    sv[i] = (row_ok && key0 + i <= vis) ? sv[i] * p.scale_log2 : -INFINITY;
+                for (int i = 0; i < 32; ++i) {
+                    sv[i] = (row_ok && key0 + i <= vis) ? sv[i] : -INFINITY;
                     mx = fmaxf(mx, sv[i]);
                 }
             }
-            red[(b * 2 + h) * kBM + r] = mx;
-            // both halves have read S tile b before either overwrites it with P
-            asm volatile("bar.sync %0, 64;" ::"r"(1 + qd) : "memory");
-            mx = fmaxf(mx, red[(b * 2 + (h ^ 1)) * kBM + r]);
+            red[cg * kBM + r] = mx;
+            // all four quarters have read S tile b (so P may overwrite it) and posted their max
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + qd) : "memory");
+            mx = fmaxf(fmaxf(red[r], red[kBM + r]), fmaxf(red[2 * kBM + r], red[3 * kBM + r]));
+            // and have read the maxima before the next tile rewrites them
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + qd) : "memory");
             if (threadIdx.x == 0) PF_TRACE(6, j);
-            const float m_new = fmaxf(m, mx);
+            const float m_new = fmaxf(m, mx * c);
             float corr = 1.f;
             if (m_new > m + kLazyRescale) {
                 corr = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
@@ -603,11 +612,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
             }
             const float m_use = (m == -INFINITY) ? 0.f : m;
             float ps = 0.f;
-            uint32_t pw[32];
+            uint32_t pw[16];
 #pragma unroll
-            for (int i = 0; i < 64; i += 2) {
-                const float a0 = fast_exp2(sv[i] - m_use);
-                const float a1 = fast_exp2(sv[i + 1] - m_use);
+            for (int i = 0; i < 32; i += 2) {
+                const float a0 = fast_exp2(fmaf(sv[i], c, -m_use));
+                const float a1 = fast_exp2(fmaf(sv[i + 1], c, -m_use));
                 ps += a0 + a1;
                 pw[i >> 1] = pack_bf16x2(a0, a1);
             }
@@ -620,9 +629,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                 }
                 tc_fence_after();
 #pragma unroll 1
-                for (int cc = 0; cc < 4; ++cc) {
+                for (int cc = 0; cc < 2; ++cc) {
                     float o[32];
-                    const uint32_t col = kTO + h * 128 + cc * 32;
+                    const uint32_t col = kTO + cg * 64 + cc * 32;
                     tmem_ld32(tmem + lane_addr + col, o);
                     tmem_wait_ld();
 #pragma unroll
@@ -630,13 +639,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                     tmem_st32(tmem + lane_addr + col, o);
                 }
             }
-            {
-                uint32_t lo[16], hi[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) { lo[i] = pw[i]; hi[i] = pw[16 + i]; }
-                tmem_st16u(tmem + lane_addr + kTS + b * kBNp + h * 32, lo);
-                tmem_st16u(tmem + lane_addr + kTS + b * kBNp + h * 32 + 16, hi);
-            }
+            tmem_st16u(tmem + lane_addr + kTS + b * kBNp + cg * 16, pw);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -647,22 +650,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
         const int jl = n_loc - 1;
         if (ok && wait_or_abort(&pv_done[jl & 1], (jl >> 1) & 1, abort_flag, 9)) {
             tc_fence_after();
-            red[h * kBM + r] = l;
-            asm volatile("bar.sync %0, 64;" ::"r"(1 + qd) : "memory");
-            const float l_row = l + red[(h ^ 1) * kBM + r];
+            red[cg * kBM + r] = l;
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + qd) : "memory");
+            const float l_row = (red[r] + red[kBM + r]) + (red[2 * kBM + r] + red[3 * kBM + r]);
             const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
             uint16_t *dst = p.out + orow * kHeadDim;
             float *part = p.nsplit > 1
                               ? p.ws + ((int64_t)blockIdx.z * T * kNumQHeads + orow) * kPartial
                               : nullptr;
-            if (part != nullptr && row_ok && h == 0) {
+            if (part != nullptr && row_ok && cg == 0) {
                 part[0] = (m == -INFINITY) ? -INFINITY : m * kLn2;
                 part[1] = l_row;
             }
 #pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = 0; cc < 2; ++cc) {
                 float o[32];
-                const int col = h * 128 + cc * 32;
+                const int col = cg * 64 + cc * 32;
                 tmem_ld32(tmem + lane_addr + kTO + col, o);
                 tmem_wait_ld();
                 if (!row_ok) continue;
