@@ -411,6 +411,57 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
     p.out[row * kHeadDim + d] = f32_to_bf16_bits(v);
 }
 
+
+// Merge for many rows with few parts (prefill key-range splits, context-parallel shards): one
+// warp per row, grid-stride; lane l owns dims [8l, 8l + 8). The same arithmetic and part order
+// as merge_kernel. A partial row is 258 floats, so its o[] is 8-byte aligned: float2 loads.
+constexpr int kMergeRowsMaxParts = 16;
+
+__global__ void __launch_bounds__(256) merge_rows_kernel(const float *parts, int64_t rows, int np,
+                                                         int64_t part_stride, const uint16_t *gate,
+                                                         uint16_t *out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * 8;
+    for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += nw) {
+        const float *base = parts + row * kPartial;
+        float ma = -INFINITY;
+        for (int c = 0; c < np; ++c) ma = fmaxf(ma, base[c * part_stride]);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float den = 0.f;
+        for (int c = 0; c < np; ++c) {
+            const float *pc = base + c * part_stride;
+            const float mc = pc[0];
+            const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - ma) * kLog2e);
+            den += pc[1] * w;
+            const float2 *o = reinterpret_cast<const float2 *>(pc + 2 + 8 * lane);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 v = o[k];
+                acc[2 * k] += v.x * w;
+                acc[2 * k + 1] += v.y * w;
+            }
+        }
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = (den == 0.f) ? 0.f : acc[k] / den;
+        if (gate) {
+            const uint4 gq = *reinterpret_cast<const uint4 *>(gate + row * kHeadDim + 8 * lane);
+            const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w};
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float g = bf16_bits_to_f32((uint16_t)(gw[k >> 1] >> ((k & 1) * 16)));
+                v[k] = v[k] * (1.0f / (1.0f + expf(-g)));
+            }
+        }
+        uint4 q;
+        q.x = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
+        q.y = (uint32_t)f32_to_bf16_bits(v[2]) | ((uint32_t)f32_to_bf16_bits(v[3]) << 16);
+        q.z = (uint32_t)f32_to_bf16_bits(v[4]) | ((uint32_t)f32_to_bf16_bits(v[5]) << 16);
+        q.w = (uint32_t)f32_to_bf16_bits(v[6]) | ((uint32_t)f32_to_bf16_bits(v[7]) << 16);
+        *reinterpret_cast<uint4 *>(out + row * kHeadDim + 8 * lane) = q;
+    }
+}
+
 }  // namespace
 
 DecodePlan decode_plan(int batch, int max_seq_len, int sm_count) {
@@ -497,6 +548,18 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
     mp.gate = gate;
     mp.out = out;
     mp.out_partial = nullptr;
+    if (num_parts <= kMergeRowsMaxParts && part_stride % 2 == 0 &&
+        (reinterpret_cast<uintptr_t>(partials) & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(gate) & 15) == 0) {
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        int64_t blocks = (rows + 7) / 8;
+        if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
+        merge_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(partials, rows, num_parts, part_stride,
+                                                               gate, out);
+        return cudaGetLastError();
+    }
     merge_kernel<<<dim3((unsigned)rows, kHeadDim / 32), kMergeWarps * 32, 0, stream>>>(mp);
     return cudaGetLastError();
 }

@@ -68,7 +68,10 @@ def test_prefill_config2_shape(cuda, oracle):
 def test_prefill_workspace_rules(cuda):
     import torch
     from peregrine_b200.capi import PgcError
-    assert cuda.prefill_workspace_bytes(24576, 1600) == 0  # config 2's pairs cover the GPU
+    # T=1152: 18 pair columns x 4 kv heads = 72 pairs, one nearly full wave on 74 pair slots
+    assert cuda.prefill_workspace_bytes(24576, 1152) == 0
+    # config 2: 100 pairs fill 68 % of two waves; two key-range shares fill 90 % of three
+    assert cuda.prefill_workspace_bytes(24576, 1600) == 2 * 1600 * NQ * 258 * 4
     P, T = 24576, 96  # 12 CTAs: the key range is split, partials need a workspace
     nbytes = cuda.prefill_workspace_bytes(P, T)
     assert nbytes > 0 and nbytes % (T * NQ * 258 * 4) == 0
