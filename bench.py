@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1-3 side figures")
     ap.add_argument("--only-configs", action="store_true",
                     help="time only the config 1-3 side figures (profiling aid)")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="profiling aid: config 2's causal prefill on one layer, 3 launches")
     return ap.parse_args()
 
 
@@ -714,6 +716,29 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def profile_prefill():
+    """One full-attention layer of config 2's prefill (1600-token chunk over a 24576-token
+    prefix, pages under a random permutation), launched 3 times: the small case for ncu
+    captures of prefill_pair_kernel (about 1 GB on the device)."""
+    import torch
+    from peregrine_b200 import capi
+    bf = torch.bfloat16
+    P, T = 24576, 1600
+    pages = (P + T + PAGE - 1) // PAGE
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    kp = torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g)
+    vp = torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g)
+    table = torch.randperm(pages, device="cuda", generator=g).to(torch.int32)
+    q = torch.randn((T, NQ, D), dtype=bf, device="cuda", generator=g)
+    out = torch.empty_like(q)
+    ws = torch.empty(max(capi.prefill_workspace_bytes(P, T), 16), dtype=torch.uint8, device="cuda")
+    for _ in range(3):
+        capi.prefill_attn(q, kp, vp, table, P, T, SCALE, out, ws)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": "prefill", "prefix": P, "chunk": T, "launches": 3}), flush=True)
+
+
 def main():
     args = parse()
     assert args.warmup >= 3 or args.impl == "reference", "at least 3 warm-up steps"
@@ -728,6 +753,9 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    if args.profile_prefill:
+        profile_prefill()
+        return
     if args.only_configs:
         import torch
         from peregrine_b200 import capi
