@@ -73,6 +73,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
+    pdl_trigger();
+    pdl_wait();
     const int split = blockIdx.x;
     const int kvh = blockIdx.y;
     const int seq = blockIdx.z;
@@ -352,6 +354,8 @@ struct MergeParams {
 constexpr int kMergeWarps = 8;
 
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergeParams p) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red_m[kMergeWarps];
     __shared__ float red_acc[kMergeWarps][32];
     __shared__ float red_den[kMergeWarps];
@@ -420,6 +424,8 @@ constexpr int kMergeRowsMaxParts = 16;
 __global__ void __launch_bounds__(256) merge_rows_kernel(const float *parts, int64_t rows, int np,
                                                          int64_t part_stride, const uint16_t *gate,
                                                          uint16_t *out) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t nw = (int64_t)gridDim.x * 8;
     for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += nw) {
@@ -514,7 +520,8 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
     sp.max_splits = plan.max_splits;
     sp.scale_log2 = scale * kLog2e;
     dim3 grid(plan.max_splits, kNumKvHeads, batch);
-    decode_split_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tk, tv, sp);
+    cudaError_t le = launch_pdl(decode_split_kernel, grid, dim3(kThreads), kSmemBytes, stream, tk, tv, sp);
+    if (le != cudaSuccess) return le;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
 
@@ -530,8 +537,8 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
     mp.out = out;
     mp.out_partial = partials_out;
     const int64_t rows = (int64_t)batch * num_queries * kNumQHeads;
-    merge_kernel<<<dim3((unsigned)rows, kHeadDim / 32), kMergeWarps * 32, 0, stream>>>(mp);
-    return cudaGetLastError();
+    return launch_pdl(merge_kernel, dim3((unsigned)rows, kHeadDim / 32), dim3(kMergeWarps * 32), 0,
+                      stream, mp);
 }
 
 cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_parts,
@@ -556,12 +563,11 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         int64_t blocks = (rows + 7) / 8;
         if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
-        merge_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(partials, rows, num_parts, part_stride,
-                                                               gate, out);
-        return cudaGetLastError();
+        return launch_pdl(merge_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, partials,
+                          rows, num_parts, part_stride, gate, out);
     }
-    merge_kernel<<<dim3((unsigned)rows, kHeadDim / 32), kMergeWarps * 32, 0, stream>>>(mp);
-    return cudaGetLastError();
+    return launch_pdl(merge_kernel, dim3((unsigned)rows, kHeadDim / 32), dim3(kMergeWarps * 32), 0,
+                      stream, mp);
 }
 
 cudaError_t decode_read_error(DevErrorHost *e, bool clear) {

@@ -43,6 +43,8 @@ struct AppendParams {
 constexpr int kRowsPerToken = kNumQHeads + kNumKvHeads;
 
 __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (gw >= p.tokens * kRowsPerToken) return;
@@ -150,7 +152,8 @@ cudaError_t launch_append(const uint16_t *q_in, int q_head_stride, uint16_t *q_o
     p.mode = mode;
     const int64_t warps = tokens * kRowsPerToken;
     const int64_t blocks = (warps + 7) / 8;
-    append_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p);
+    cudaError_t e = launch_pdl(append_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, p);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -87,6 +87,39 @@ __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with launch_pdl may start while the
+// previous kernel in its stream is still running; pdl_wait() blocks until that kernel has
+// completed and its memory is visible, so every such kernel calls it before its first global
+// memory access (whatever precedes it in the stream). pdl_trigger() lets the next kernel
+// launch once every CTA of this grid has started.
+#ifndef PGC_NO_PDL
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+#else  // build option: plain stream-ordered launches
+__device__ __forceinline__ void pdl_wait() {}
+__device__ __forceinline__ void pdl_trigger() {}
+#endif
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+#ifndef PGC_NO_PDL
+    cfg.numAttrs = 1;
+#else
+    cfg.numAttrs = 0;
+#endif
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
