@@ -464,6 +464,48 @@ int pgc_prefix_cache_finish_loaded(pgc_prefix_cache *cache, pgc_match match);
 /* persistedEntryConst (:153-163): the active entry, else the most recently used one. */
 int pgc_prefix_cache_persisted(const pgc_prefix_cache *cache, pgc_match *out);
 
+/* ---------------------------------------------------------------------------------------
+ * Linear attention (Gated-DeltaNet) state producers: the causal conv1d + SiLU and the gated
+ * delta-rule recurrence, for the 24 linear layers whose states pgc_copy_regions snapshots,
+ * restores and rolls back. Shapes are the model's (src/model/block_linear.zig:18-26).
+ * Per sequence: conv state f32 [3][8192] (oldest first), recurrent state f32 [32][128][128]
+ * ([Hv][Dv][Dk]); conv_out rows are [q 2048 | k 2048 | v 4096] bf16. Decode entries take a
+ * batch of sequences whose states live in slot arrays (`slots` [batch] int32 device indices;
+ * NULL = sequence i uses slot i) and update them in place.
+ * ------------------------------------------------------------------------------------- */
+#define PGC_LIN_KEY_HEADS 16
+#define PGC_LIN_VALUE_HEADS 32
+#define PGC_LIN_HEAD_DIM 128
+#define PGC_LIN_CONV_DIM 8192
+#define PGC_LIN_CONV_KERNEL 4
+
+/* conv1d_silu_decode_bf16 (shaders/conv1d.metal:49-66): x [batch][8192] bf16, weight
+ * [8192][4] bf16 (8-byte aligned), out [batch][8192] bf16; conv_states [num_slots][3][8192]. */
+int pgc_conv1d_decode(float *conv_states, int64_t num_slots, const int32_t *slots, int batch,
+                      const uint16_t *x, const uint16_t *weight, uint16_t *out, void *stream);
+
+/* conv1d_silu_prefill_vec4_bf16 + conv1d_silu_prefill_state_bf16 (conv1d.metal:128-186) for one
+ * sequence: x/out [tokens][8192] bf16; the state is read (has_previous_state) then published. */
+int pgc_conv1d_prefill(float *conv_state, int has_previous_state, const uint16_t *x, int tokens,
+                       const uint16_t *weight, uint16_t *out, void *stream);
+
+/* gated_delta_decode_h128_fused_bf16 (shaders/gated_delta.metal:146-261) over a batch: conv_out
+ * [batch][8192] bf16 (16-byte aligned), a/b [batch][32] bf16, a_log [32] f32, dt_bias [32] bf16,
+ * y [batch][4096] bf16; states [num_slots][32][128][128] f32 updated in place. */
+int pgc_gated_delta_decode(float *states, int64_t num_slots, const int32_t *slots, int batch,
+                           int has_previous_state, const uint16_t *conv_out, const uint16_t *a,
+                           const uint16_t *b, const float *a_log, const uint16_t *dt_bias,
+                           uint16_t *y, void *stream);
+
+/* Prefill of one sequence (src/model/block_linear.zig:335-346: qk_l2norm_prefill_bf16,
+ * gating_many_bf16, gated_delta_prefill_h128_norm_prepared_value_major_r8_bf16): conv_out
+ * [tokens][8192], a/b [tokens][32], y [tokens][4096]. Workspace: normalised q/k and gates. */
+size_t pgc_gated_delta_prefill_workspace_bytes(int tokens);
+int pgc_gated_delta_prefill(float *state, int has_previous_state, const uint16_t *conv_out,
+                            const uint16_t *a, const uint16_t *b, const float *a_log,
+                            const uint16_t *dt_bias, int tokens, uint16_t *y, void *workspace,
+                            size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

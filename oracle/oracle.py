@@ -46,14 +46,18 @@ _SIG = {
     "pgo_kv_copy_tokens": (I32, [P, P, I64, P, I64, I64, P, P, I64, P, I64, I64, I64]),
     "pgo_copy_rows": (None, [P, P, P, P, I64, I64, I64, I64]),
     "pgo_rollback": (None, [P, P, I32, I32, P, P, P, I32]),
+    "pgo_conv1d_decode": (None, [P, P, P, P, I32, I32]),
+    "pgo_conv1d_prefill": (None, [P, I32, P, I32, P, P, I32, I32]),
+    "pgo_gated_delta_decode": (None, [P, I32, P, P, P, P, P, P]),
+    "pgo_gated_delta_prefill": (None, [P, I32, P, P, P, P, P, I32, P]),
 }
 
 _lib = None
 
 
 def build() -> Path:
-    src = HERE / "pgo_oracle.c"
-    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+    newest = max((HERE / f).stat().st_mtime for f in ("pgo_oracle.c", "pgo_linear.c", "pgo_oracle.h"))
+    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < newest:
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB_PATH
 
@@ -206,3 +210,40 @@ def rollback(accept, seq_lens, seq_index, reject_tokens, pairs):
     srcs = (C.c_void_p * max(1, n))(*[_p(s) for _, s in pairs])
     nbytes = (C.c_uint64 * max(1, n))(*[d.nbytes for d, _ in pairs])
     lib().pgo_rollback(_p(accept), _p(seq_lens), seq_index, reject_tokens, dsts, srcs, nbytes, n)
+
+
+# ------------------------------------------------------------------ linear attention (pgo_linear.c)
+LIN_CONV, LIN_K, LIN_HV, LIN_DV, LIN_DK = 8192, 4, 32, 128, 128
+
+
+def conv1d_decode(state, x, w):
+    """state f32 [3][8192] (updated in place), x bf16 [8192], w bf16 [8192][4] -> out bf16."""
+    out = np.empty(LIN_CONV, np.uint16)
+    lib().pgo_conv1d_decode(_p(state), _p(x), _p(w), _p(out), LIN_CONV, LIN_K)
+    return out
+
+
+def conv1d_prefill(state, has_state, x, w):
+    """x bf16 [T][8192] -> out bf16 [T][8192]; state published in place."""
+    T = x.shape[0]
+    out = np.empty((T, LIN_CONV), np.uint16)
+    lib().pgo_conv1d_prefill(_p(state), int(has_state), _p(x), T, _p(w), _p(out), LIN_CONV, LIN_K)
+    return out
+
+
+def gated_delta_decode(state, has_state, conv_out, a, b, a_log, dt_bias):
+    """state f32 [32][128][128] in place; returns y bf16 [4096]."""
+    y = np.empty(LIN_HV * LIN_DV, np.uint16)
+    lib().pgo_gated_delta_decode(_p(state), int(has_state), _p(conv_out), _p(a), _p(b), _p(a_log),
+                                 _p(dt_bias), _p(y))
+    return y
+
+
+def gated_delta_prefill(state, has_state, conv_out, a, b, a_log, dt_bias):
+    """conv_out bf16 [T][8192], a/b bf16 [T][32]; returns y bf16 [T][4096]."""
+    T = conv_out.shape[0]
+    y = np.empty((T, LIN_HV * LIN_DV), np.uint16)
+    lib().pgo_gated_delta_prefill(_p(state), int(has_state), _p(conv_out), _p(a), _p(b), _p(a_log),
+                                  _p(dt_bias), T, _p(y))
+    return y
+

@@ -105,6 +105,19 @@ void pgo_copy_rows(void *dst, const void *src, const int32_t *dst_rows, const in
 void pgo_rollback(const int32_t *accept, int32_t *seq_lens, int seq_index, int reject_tokens,
                   void *const *dsts, const void *const *srcs, const uint64_t *bytes, int n);
 
+/* Linear attention (pgo_linear.c): conv1d + SiLU, gated delta-rule recurrence. Shapes fixed to
+ * the model's (Hk 16, Hv 32, Dk = Dv = 128, conv_dim 8192). */
+void pgo_conv1d_decode(float *state, const uint16_t *x, const uint16_t *w, uint16_t *out, int C,
+                       int K);
+void pgo_conv1d_prefill(float *state, int has_state, const uint16_t *x, int T, const uint16_t *w,
+                        uint16_t *out, int C, int K);
+void pgo_gated_delta_decode(float *state, int has_state, const uint16_t *conv_out, const uint16_t *a,
+                            const uint16_t *b, const float *A_log, const uint16_t *dt_bias,
+                            uint16_t *y);
+void pgo_gated_delta_prefill(float *state, int has_state, const uint16_t *conv_out, const uint16_t *a,
+                             const uint16_t *b, const float *A_log, const uint16_t *dt_bias, int T,
+                             uint16_t *y);
+
 #ifdef __cplusplus
 }
 #endif

@@ -119,6 +119,11 @@ SIGNATURES = {
     "pgc_prefix_file_read": (I32, [C.c_char_p, U64, U64, U64, P, U64, C.POINTER(PrefixInfo)]),
     "pgc_prefix_file_header": (I32, [P, U64, U64, U64, C.c_uint32, I32, I32]),
     "pgc_prefix_file_write": (I32, [C.c_char_p, P, U64]),
+    "pgc_conv1d_decode": (I32, [P, I64, P, I32, P, P, P, P]),
+    "pgc_conv1d_prefill": (I32, [P, I32, P, I32, P, P, P]),
+    "pgc_gated_delta_decode": (I32, [P, I64, P, I32, I32, P, P, P, P, P, P, P]),
+    "pgc_gated_delta_prefill_workspace_bytes": (SZ, [I32]),
+    "pgc_gated_delta_prefill": (I32, [P, I32, P, P, P, P, P, I32, P, P, SZ, P]),
     "pgc_page_pool_create": (P, [I32]),
     "pgc_page_pool_destroy": (None, [P]),
     "pgc_page_pool_alloc": (I32, [P, I32, P]),
@@ -369,3 +374,46 @@ def prefix_file_header(image_ptr: int, image_bytes: int, fingerprint: int, token
 def prefix_file_write(path, image_ptr: int, image_bytes: int) -> None:
     check(lib().pgc_prefix_file_write(str(path).encode(), image_ptr, image_bytes),
           "pgc_prefix_file_write")
+
+
+# ----------------------------------------------------------------------------- linear attention
+LIN_CONV_DIM = 8192
+LIN_VALUE_HEADS = 32
+LIN_HEAD_DIM = 128
+
+
+def conv1d_decode(conv_states, x, weight, out, slots=None, stream=None) -> None:
+    """conv_states f32 [num_slots][3][8192]; x/out [batch][8192] bf16; slots [batch] int32."""
+    batch = x.shape[0]
+    check(lib().pgc_conv1d_decode(_ptr(conv_states), conv_states.shape[0], _ptr(slots), batch,
+                                  _ptr(x), _ptr(weight), _ptr(out), _stream(stream)),
+          "pgc_conv1d_decode")
+
+
+def conv1d_prefill(conv_state, has_previous_state, x, weight, out, stream=None) -> None:
+    check(lib().pgc_conv1d_prefill(_ptr(conv_state), int(has_previous_state), _ptr(x), x.shape[0],
+                                   _ptr(weight), _ptr(out), _stream(stream)), "pgc_conv1d_prefill")
+
+
+def gated_delta_decode(states, has_previous_state, conv_out, a, b, a_log, dt_bias, y, slots=None,
+                       stream=None) -> None:
+    """states f32 [num_slots][32][128][128]; conv_out [batch][8192]; a/b [batch][32]; y
+    [batch][4096]."""
+    batch = conv_out.shape[0]
+    check(lib().pgc_gated_delta_decode(_ptr(states), states.shape[0], _ptr(slots), batch,
+                                       int(has_previous_state), _ptr(conv_out), _ptr(a), _ptr(b),
+                                       _ptr(a_log), _ptr(dt_bias), _ptr(y), _stream(stream)),
+          "pgc_gated_delta_decode")
+
+
+def gated_delta_prefill_workspace_bytes(tokens: int) -> int:
+    return lib().pgc_gated_delta_prefill_workspace_bytes(tokens)
+
+
+def gated_delta_prefill(state, has_previous_state, conv_out, a, b, a_log, dt_bias, y, workspace,
+                        stream=None) -> None:
+    check(lib().pgc_gated_delta_prefill(_ptr(state), int(has_previous_state), _ptr(conv_out), _ptr(a),
+                                        _ptr(b), _ptr(a_log), _ptr(dt_bias), conv_out.shape[0], _ptr(y),
+                                        _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                        _stream(stream)), "pgc_gated_delta_prefill")
+

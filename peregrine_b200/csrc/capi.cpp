@@ -176,15 +176,16 @@ int pgc_device_error(int *code_out, int64_t *detail_out, int clear) {
     int st = check_device(nullptr);
     if (st != PGC_OK) return st;
     if (cudaDeviceSynchronize() != cudaSuccess) return PGC_ERR_CUDA;
-    DevErrorHost e[4] = {};
+    DevErrorHost e[5] = {};
     cudaError_t r = decode_read_error(&e[0], clear != 0);
     if (r == cudaSuccess) r = append_read_error(&e[1], clear != 0);
     if (r == cudaSuccess) r = copy_read_error(&e[2], clear != 0);
     if (r == cudaSuccess) r = prefill_read_error(&e[3], clear != 0);
+    if (r == cudaSuccess) r = linear_read_error(&e[4], clear != 0);
     if (r != cudaSuccess) return PGC_ERR_CUDA;
     int code = 0;
     long long detail = 0;
-    for (int i = 0; i < 4 && code == 0; ++i)
+    for (int i = 0; i < 5 && code == 0; ++i)
         if (e[i].code != 0) {
             code = e[i].code + 100 * i;  // unit in the hundreds digit
             detail = e[i].detail;
@@ -471,6 +472,68 @@ int pgc_rollback(const int32_t *accept, int32_t *seq_lens, int seq_index, int re
     if (!accept || !seq_lens || seq_index < 0 || reject_tokens < 0) return PGC_ERR_INVALID;
     return cuda_status(launch_regions(regions_host, n, false, accept, seq_lens, seq_index,
                                       reject_tokens, static_cast<cudaStream_t>(stream)));
+}
+
+// ------------------------------------------------------------------ linear attention
+int pgc_conv1d_decode(float *conv_states, int64_t num_slots, const int32_t *slots, int batch,
+                      const uint16_t *x, const uint16_t *weight, uint16_t *out, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (batch < 0 || num_slots <= 0) return PGC_ERR_INVALID;
+    if (batch == 0) return PGC_OK;
+    if (!conv_states || !x || !weight || !out) return PGC_ERR_INVALID;
+    if (!slots && batch > num_slots) return PGC_ERR_BOUNDS;
+    if (((uintptr_t)weight & 7u) != 0 || ((uintptr_t)conv_states & 3u) != 0) return PGC_ERR_ALIGN;
+    return cuda_status(launch_conv1d_decode(conv_states, num_slots, slots, batch, x, weight, out,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_conv1d_prefill(float *conv_state, int has_previous_state, const uint16_t *x, int tokens,
+                       const uint16_t *weight, uint16_t *out, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (tokens < 0) return PGC_ERR_INVALID;
+    if (tokens == 0) return PGC_OK;
+    if (!conv_state || !x || !weight || !out) return PGC_ERR_INVALID;
+    if (((uintptr_t)weight & 7u) != 0 || ((uintptr_t)conv_state & 3u) != 0) return PGC_ERR_ALIGN;
+    return cuda_status(launch_conv1d_prefill(conv_state, has_previous_state != 0, x, tokens, weight, out,
+                                             static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_gated_delta_decode(float *states, int64_t num_slots, const int32_t *slots, int batch,
+                           int has_previous_state, const uint16_t *conv_out, const uint16_t *a,
+                           const uint16_t *b, const float *a_log, const uint16_t *dt_bias,
+                           uint16_t *y, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (batch < 0 || num_slots <= 0) return PGC_ERR_INVALID;
+    if (batch == 0) return PGC_OK;
+    if (!states || !conv_out || !a || !b || !a_log || !dt_bias || !y) return PGC_ERR_INVALID;
+    if (!slots && batch > num_slots) return PGC_ERR_BOUNDS;
+    if (!al16(conv_out) || ((uintptr_t)states & 3u) != 0) return PGC_ERR_ALIGN;
+    return cuda_status(launch_gated_delta_decode(states, num_slots, slots, batch, has_previous_state != 0,
+                                                 conv_out, a, b, a_log, dt_bias, y,
+                                                 static_cast<cudaStream_t>(stream)));
+}
+
+size_t pgc_gated_delta_prefill_workspace_bytes(int tokens) {
+    return gated_delta_prefill_workspace_bytes(tokens);
+}
+
+int pgc_gated_delta_prefill(float *state, int has_previous_state, const uint16_t *conv_out,
+                            const uint16_t *a, const uint16_t *b, const float *a_log,
+                            const uint16_t *dt_bias, int tokens, uint16_t *y, void *workspace,
+                            size_t workspace_bytes, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (tokens < 0) return PGC_ERR_INVALID;
+    if (tokens == 0) return PGC_OK;
+    if (!state || !conv_out || !a || !b || !a_log || !dt_bias || !y || !workspace) return PGC_ERR_INVALID;
+    if (workspace_bytes < gated_delta_prefill_workspace_bytes(tokens)) return PGC_ERR_WORKSPACE;
+    if (!al16(conv_out) || !al16(workspace) || ((uintptr_t)state & 3u) != 0) return PGC_ERR_ALIGN;
+    return cuda_status(launch_gated_delta_prefill(state, has_previous_state != 0, conv_out, a, b, a_log,
+                                                  dt_bias, tokens, y, workspace,
+                                                  static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

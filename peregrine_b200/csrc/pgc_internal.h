@@ -80,4 +80,21 @@ cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUten
                            int sm_count, cudaStream_t stream);
 cudaError_t prefill_read_error(DevErrorHost *e, bool clear);
 
+// linear_attn.cu
+size_t gated_delta_prefill_workspace_bytes(int tokens);
+cudaError_t launch_conv1d_decode(float *states, int64_t num_slots, const int32_t *slots, int batch,
+                                 const uint16_t *x, const uint16_t *w, uint16_t *out,
+                                 cudaStream_t stream);
+cudaError_t launch_conv1d_prefill(float *state, int has_state, const uint16_t *x, int T,
+                                  const uint16_t *w, uint16_t *out, cudaStream_t stream);
+cudaError_t launch_gated_delta_decode(float *states, int64_t num_slots, const int32_t *slots, int batch,
+                                      int has_state, const uint16_t *conv_out, const uint16_t *a,
+                                      const uint16_t *b, const float *a_log, const uint16_t *dt_bias,
+                                      uint16_t *y, cudaStream_t stream);
+cudaError_t launch_gated_delta_prefill(float *state, int has_state, const uint16_t *conv_out,
+                                       const uint16_t *a, const uint16_t *b, const float *a_log,
+                                       const uint16_t *dt_bias, int T, uint16_t *y, void *ws,
+                                       cudaStream_t stream);
+cudaError_t linear_read_error(DevErrorHost *e, bool clear);
+
 }  // namespace pgc
