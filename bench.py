@@ -476,6 +476,60 @@ def bench_config3(capi, iters=10):
             "GB_s": round(moved / (ms * 1e-3) / 1e9, 1)}
 
 
+def bench_linear(capi, iters=10):
+    """The linear-attention state producers (24 Gated-DeltaNet layers; no BASELINE config names
+    them, they write the states configs 2-3 restore). Decode: 64 sequences, one token each, per
+    layer a conv1d step and a gated delta-rule step over slot-indexed states (each sequence's
+    2 MiB recurrent state read and written once, conv state 96 KiB). Prefill: one 1600-token
+    chunk of one sequence through both. The q4 projections around them are out of scope:
+    conv inputs, a/b and the gate parameters are seeded N(0,1) bf16."""
+    import torch
+    bf = torch.bfloat16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    B, LAYERS_LIN, T = 64, 24, 1600
+    C, HV = capi.LIN_CONV_DIM, capi.LIN_VALUE_HEADS
+    rec = [torch.randn((B, HV, 128, 128), device="cuda", generator=g) * 0.05 for _ in range(LAYERS_LIN)]
+    conv = [torch.randn((B, 3, C), device="cuda", generator=g) for _ in range(LAYERS_LIN)]
+    w = torch.randn((C, 4), dtype=bf, device="cuda", generator=g)
+    x = torch.randn((B, C), dtype=bf, device="cuda", generator=g)
+    co = torch.empty_like(x)
+    a = torch.randn((B, HV), dtype=bf, device="cuda", generator=g)
+    b = torch.randn((B, HV), dtype=bf, device="cuda", generator=g)
+    a_log = torch.randn(HV, device="cuda", generator=g) * 0.5 - 1.0
+    dtb = torch.randn(HV, dtype=bf, device="cuda", generator=g)
+    y = torch.empty((B, HV * 128), dtype=bf, device="cuda")
+    s = torch.cuda.current_stream()
+
+    def decode_step():
+        for l in range(LAYERS_LIN):
+            capi.conv1d_decode(conv[l], x, w, co, stream=s)
+            capi.gated_delta_decode(rec[l], True, co, a, b, a_log, dtb, y, stream=s)
+
+    dec_ms = _ev_time(decode_step, iters)
+    dec_bytes = LAYERS_LIN * B * (2 * HV * 128 * 128 * 4 + 2 * 3 * C * 4 + 3 * C * 2 + 2 * HV * 128 * 2)
+    xs = torch.randn((T, C), dtype=bf, device="cuda", generator=g)
+    cs = torch.empty_like(xs)
+    at = torch.randn((T, HV), dtype=bf, device="cuda", generator=g)
+    bt = torch.randn((T, HV), dtype=bf, device="cuda", generator=g)
+    yt = torch.empty((T, HV * 128), dtype=bf, device="cuda")
+    ws = torch.empty(capi.gated_delta_prefill_workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    st1 = [r[0] for r in rec]
+    cv1 = [c_[0] for c_ in conv]
+
+    def prefill_chunk():
+        for l in range(LAYERS_LIN):
+            capi.conv1d_prefill(cv1[l], True, xs, w, cs, stream=s)
+            capi.gated_delta_prefill(st1[l], True, cs, at, bt, a_log, dtb, yt, ws, stream=s)
+
+    pf_ms = _ev_time(prefill_chunk, max(2, iters // 4))
+    return {"workload": "24 linear layers: decode of 64 sequences (conv1d + gated delta rule over "
+                        "slot-indexed states); prefill of one 1600-token chunk",
+            "decode_ms_per_step": round(dec_ms, 4), "decode_state_bytes": dec_bytes,
+            "decode_GB_s": round(dec_bytes / (dec_ms * 1e-3) / 1e9, 1),
+            "prefill_ms_per_chunk": round(pf_ms, 3)}
+
+
 def bench_config5b(capi, rank, world, iters=20, warmup=3):
     """Config 5b: one 262144-token sequence (8 layers, 16q/4kv, d=256), context-parallel across
     the ranks in contiguous page-aligned KV shards; per layer: q/k RoPE (the new K/V row lands
@@ -707,7 +761,7 @@ def run_ours(args, rank, world, local_rank):
         line["configs"] = {"config5b": cfg5b}
         if world == 1:
             line["configs"].update({"config1": bench_config1(capi), "config2": bench_config2(capi),
-                                    "config3": bench_config3(capi)})
+                                    "config3": bench_config3(capi), "linear": bench_linear(capi)})
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         gbs, dt, desc = cpu_sample(lens, threads, max_tokens=1 << 30, min_seconds=10.0)
@@ -761,7 +815,7 @@ def main():
         from peregrine_b200 import capi
         torch.cuda.set_device(local_rank)
         print(json.dumps({"configs": {"config1": bench_config1(capi), "config2": bench_config2(capi),
-                                      "config3": bench_config3(capi),
+                                      "config3": bench_config3(capi), "linear": bench_linear(capi),
                                       "config5b": bench_config5b(capi, 0, 1)}}), flush=True)
         return
     try:

@@ -142,13 +142,27 @@ __global__ void __launch_bounds__(256) conv1d_publish_kernel(float *state, int h
 
 // ---------------------------------------------------------------- gated delta rule
 // One warp's 8 value rows of head hv for one token: decay, rank-1 delta update, y. q/k are this
-// lane's 4 normalised key values, kq their full dot product. state rows in registers.
-__device__ __forceinline__ void delta_rows(float (&st)[kRowsPerWarp][4], const float (&q)[4],
-                                           const float (&k)[4], float kq, const float (&v)[kRowsPerWarp],
-                                           float decay, float beta, uint16_t *y, int lane) {
-    float kv[kRowsPerWarp], ob[kRowsPerWarp];
+// lane's 4 normalised key values, kq their full dot product; state rows in registers.
+//
+// The 16 row sums (kv_mem and the y base of 8 rows) are reduced with a reduce-scatter over the
+// warp instead of 16 butterflies: at each xor stage (16, 8, 4, 2) a lane keeps half of its
+// values and adds the partner's copy of that half, then xor 1 completes the sum. Every stage
+// adds the same operand pairs a butterfly would (fp addition is commutative), so each result is
+// bitwise the butterfly's; lane l ends with value 8*b4 + 4*b3 + 2*b2 + b1 of its bits. The lane
+// holding kv_mem[r] forms delta[r], the y lane (l ^ 16) receives it, and the 8 deltas are then
+// broadcast for the state update: 25 shuffles per token instead of 80.
+template <int R>
+__device__ __forceinline__ void delta_rows(float (&st)[R][4], const float (&q)[4], const float (&k)[4],
+                                           float kq, const float (&v)[R], float decay, float beta,
+                                           uint16_t *y, int lane) {
+    // S scatter stages (xor 16, 8, ...) halve 2R values to one; the remaining xor offsets finish
+    // as a butterfly. Lane l then holds value idx = sum_i bit(16 >> i) * 2^(S-1-i): kv_mem[idx]
+    // when b4 = 0, the y base of row idx - R when b4 = 1.
+    constexpr int S = R == 8 ? 4 : (R == 4 ? 3 : (R == 2 ? 2 : 1));
+    static_assert((2 << (S - 1)) == 2 * R, "R is 1, 2, 4 or 8");
+    float acc[2 * R];
 #pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r) {
+    for (int r = 0; r < R; ++r) {
         float sk = 0.0f, sq = 0.0f;
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
@@ -156,20 +170,41 @@ __device__ __forceinline__ void delta_rows(float (&st)[kRowsPerWarp][4], const f
             sk = __fadd_rn(sk, __fmul_rn(st[r][ch], k[ch]));
             sq = __fadd_rn(sq, __fmul_rn(st[r][ch], q[ch]));
         }
-        kv[r] = sk;
-        ob[r] = sq;
+        acc[r] = sk;
+        acc[R + r] = sq;
     }
 #pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r) {
-        kv[r] = warp_sum(kv[r]);
-        ob[r] = warp_sum(ob[r]);
-    }
+    for (int st_i = 0; st_i < S; ++st_i) {
+        const int n = (2 * R) >> st_i, o = 16 >> st_i;
+        const bool hi = (lane & o) != 0;
 #pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r) {
-        const float delta = __fmul_rn(__fsub_rn(v[r], kv[r]), beta);
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = hi ? acc[i] : acc[i + n / 2];
+            const float keep = hi ? acc[i + n / 2] : acc[i];
+            acc[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+        }
+    }
+    float sum = acc[0];
+#pragma unroll
+    for (int o = 16 >> S; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    int r_mine = 0;
+#pragma unroll
+    for (int i = 1; i < S; ++i) r_mine |= ((lane >> (4 - i)) & 1) << (S - 1 - i);
+    float vr = v[0];
+#pragma unroll
+    for (int r = 1; r < R; ++r) vr = r == r_mine ? v[r] : vr;
+    const float delta_mine = __fmul_rn(__fsub_rn(vr, sum), beta);  // meaningful on b4 = 0 lanes
+    const float delta_y = __shfl_xor_sync(0xffffffffu, delta_mine, 16);
+    if ((lane & 16) && (lane & ((16 >> (S - 1)) - 1)) == 0)
+        y[r_mine] = f32_to_bf16_bits(__fadd_rn(sum, __fmul_rn(delta_y, kq)));
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        int src = 0;
+#pragma unroll
+        for (int i = 1; i < S; ++i) src |= ((r >> (S - 1 - i)) & 1) << (4 - i);
+        const float delta = __shfl_sync(0xffffffffu, delta_mine, src);
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) st[r][ch] = __fadd_rn(st[r][ch], __fmul_rn(k[ch], delta));
-        if (lane == 0) y[r] = f32_to_bf16_bits(__fadd_rn(ob[r], __fmul_rn(delta, kq)));
     }
 }
 
@@ -225,7 +260,7 @@ __global__ void __launch_bounds__(kWarps * 32) gated_delta_decode_kernel(
     const uint32_t vw[4] = {vq.x, vq.y, vq.z, vq.w};
 #pragma unroll
     for (int r = 0; r < kRowsPerWarp; ++r) v[r] = bf((uint16_t)(vw[r >> 1] >> ((r & 1) * 16)));
-    delta_rows(st, q, k, kq, v, decay, beta, y + (int64_t)s * kValDim + hv * kDv + dv0, lane);
+    delta_rows<kRowsPerWarp>(st, q, k, kq, v, decay, beta, y + (int64_t)s * kValDim + hv * kDv + dv0, lane);
 #pragma unroll
     for (int r = 0; r < kRowsPerWarp; ++r)
 #pragma unroll
@@ -233,14 +268,16 @@ __global__ void __launch_bounds__(kWarps * 32) gated_delta_decode_kernel(
 }
 
 // qk_l2norm_prefill_bf16 (gated_norm.metal:191-245) and gating_many_bf16 (:247-263) for one
-// sequence: block (token, key head) of 128 threads with the same shared-memory tree; it also
-// writes the gates of value heads 2hk and 2hk+1. ws: q, k f32 [T][16][128], g, beta f32 [T][32].
+// sequence: block (token, key head) of 128 threads with the same shared-memory tree. Outputs are
+// head-major so that the scan stages a chunk of tokens with contiguous copies: q, k f32
+// [16][T][128]; kq f32 [16][T] (q.k of the normalised vectors, lane-chunk order then the warp
+// butterfly, as the scan would form it); g, beta f32 [32][T] (value heads 2hk and 2hk+1).
 __global__ void __launch_bounds__(128) gated_delta_prep_kernel(const uint16_t *conv_out,
                                                                const uint16_t *a, const uint16_t *b,
                                                                const float *a_log,
                                                                const uint16_t *dt_bias, int T,
-                                                               float *qn, float *kn, float *g,
-                                                               float *beta) {
+                                                               float *qn, float *kn, float *kqn,
+                                                               float *g, float *beta) {
     pdl_trigger();
     pdl_wait();
     __shared__ float pq[128], pk[128];
@@ -261,77 +298,130 @@ __global__ void __launch_bounds__(128) gated_delta_prep_kernel(const uint16_t *c
     const float q_inv = inv_sqrt(__fadd_rn(pq[0], 1.0e-6f));
     const float k_inv = inv_sqrt(__fadd_rn(pk[0], 1.0e-6f));
     const float q_scale = inv_sqrt((float)kDk);
-    const int64_t o = ((int64_t)t * kHk + hk) * kDk + tid;
-    qn[o] = __fmul_rn(__fmul_rn(qv, q_inv), q_scale);
-    kn[o] = __fmul_rn(kv, k_inv);
-    if (tid < 2) {
-        const int hv = 2 * hk + tid;
-        float d, bt;
-        gates(bf(a[(int64_t)t * kHv + hv]), bf(dt_bias[hv]), a_log[hv], bf(b[(int64_t)t * kHv + hv]), &d, &bt);
-        g[(int64_t)t * kHv + hv] = d;
-        beta[(int64_t)t * kHv + hv] = bt;
+    const float qo = __fmul_rn(__fmul_rn(qv, q_inv), q_scale);
+    const float ko = __fmul_rn(kv, k_inv);
+    const int64_t o = ((int64_t)hk * T + t) * kDk + tid;
+    qn[o] = qo;
+    kn[o] = ko;
+    __syncthreads();  // the tree is done with pq: reuse it for q.k
+    pq[tid] = __fmul_rn(ko, qo);
+    __syncthreads();
+    if (tid < 32) {
+        float sacc = 0.0f;
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) sacc = __fadd_rn(sacc, pq[tid + 32 * ch]);
+        sacc = warp_sum(sacc);
+        if (tid == 0) kqn[(int64_t)hk * T + t] = sacc;
+        if (tid < 2) {
+            const int hv = 2 * hk + tid;
+            float d, bt;
+            gates(bf(a[(int64_t)t * kHv + hv]), bf(dt_bias[hv]), a_log[hv], bf(b[(int64_t)t * kHv + hv]), &d, &bt);
+            g[(int64_t)hv * T + t] = d;
+            beta[(int64_t)hv * T + t] = bt;
+        }
     }
 }
 
 // gated_delta_prefill_h128_norm_prepared_value_major_r8_bf16 (gated_delta.metal:35-138): the
-// scan over T tokens of one sequence with each warp's 8 state rows held in registers; the next
-// token's inputs are loaded while the current one is computed.
-__global__ void __launch_bounds__(kWarps * 32) gated_delta_scan_kernel(
+// scan over T tokens of one sequence, state rows in registers. The token loop is sequential, so
+// what bounds it is the latency of one token's update; the inputs every warp of a head needs
+// (q, k, q.k, gates) are staged once per CTA in shared memory, 64 tokens at a time and double
+// buffered with cp.async, instead of being re-read from L2 by each warp. CTA = 32 value rows of
+// one head (8 warps x 4 rows); grid 4 x 32 = 128 CTAs, one per SM: per token each SM issues the
+// ~180 instructions of each of its 8 warps, and more rows per SM would make issue the bound.
+constexpr int kScanRows = 4;
+constexpr int kScanWarps = 8;
+constexpr int kScanRowsPerCta = kScanRows * kScanWarps;
+constexpr int kScanChunk = 64;
+struct ScanStage {
+    float q[kScanChunk][kDk];
+    float k[kScanChunk][kDk];
+    float kq[kScanChunk];
+    float g[kScanChunk];
+    float beta[kScanChunk];
+    uint16_t v[kScanChunk][kScanRowsPerCta];
+};
+constexpr int kScanSmem = 2 * (int)sizeof(ScanStage);
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *smem_dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
+}
+
+__global__ void __launch_bounds__(kScanWarps * 32) gated_delta_scan_kernel(
     float *state, int has_state, const uint16_t *conv_out, const float *qn, const float *kn,
-    const float *g, const float *beta, int T, uint16_t *y) {
+    const float *kqn, const float *g, const float *beta, int T, uint16_t *y) {
     pdl_trigger();
     pdl_wait();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    extern __shared__ __align__(16) uint8_t scan_smem[];
+    ScanStage *stage = reinterpret_cast<ScanStage *>(scan_smem);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
     const int hv = blockIdx.y;
     const int hk = hv / (kHv / kHk);
-    const int dv0 = blockIdx.x * kRowsPerCta + warp * kRowsPerWarp;
+    const int row0 = blockIdx.x * kScanRowsPerCta;
+    const int dv0 = row0 + warp * kScanRows;
     float *st_g = state + ((int64_t)hv * kDv + dv0) * kDk;
-    float st[kRowsPerWarp][4];
+    float st[kScanRows][4];
 #pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r)
+    for (int r = 0; r < kScanRows; ++r)
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) st[r][ch] = has_state ? st_g[r * kDk + lane + 32 * ch] : 0.0f;
 
-    auto load = [&](int t, float (&q)[4], float (&k)[4], uint4 &vq, float &dc, float &bt) {
-        const int64_t o = ((int64_t)t * kHk + hk) * kDk + lane;
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-            q[ch] = qn[o + 32 * ch];
-            k[ch] = kn[o + 32 * ch];
+    const int n_chunks = (T + kScanChunk - 1) / kScanChunk;
+    auto issue = [&](int c) {
+        ScanStage &sg = stage[c & 1];
+        const int t0 = c * kScanChunk;
+        const int n = min(kScanChunk, T - t0);
+        const float *qs = qn + ((int64_t)hk * T + t0) * kDk;
+        const float *ks = kn + ((int64_t)hk * T + t0) * kDk;
+        for (int i = tid; i < n * (kDk / 4); i += kScanWarps * 32) {
+            cp_async16(&sg.q[0][0] + 4 * i, qs + 4 * i);
+            cp_async16(&sg.k[0][0] + 4 * i, ks + 4 * i);
         }
-        vq = *reinterpret_cast<const uint4 *>(conv_out + (int64_t)t * kConv + 2 * kKeyDim + hv * kDv + dv0);
-        dc = g[(int64_t)t * kHv + hv];
-        bt = beta[(int64_t)t * kHv + hv];
+        for (int i = tid; i < n; i += kScanWarps * 32) {
+            cp_async4(&sg.kq[i], kqn + (int64_t)hk * T + t0 + i);
+            cp_async4(&sg.g[i], g + (int64_t)hv * T + t0 + i);
+            cp_async4(&sg.beta[i], beta + (int64_t)hv * T + t0 + i);
+        }
+        // v: this CTA's 64 rows of each token = 128 contiguous bytes of conv_out
+        for (int i = tid; i < n * (kScanRowsPerCta / 8); i += kScanWarps * 32) {
+            const int tt = i / (kScanRowsPerCta / 8), u = i % (kScanRowsPerCta / 8);
+            cp_async16(&sg.v[tt][8 * u],
+                       conv_out + (int64_t)(t0 + tt) * kConv + 2 * kKeyDim + hv * kDv + row0 + 8 * u);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    float q[4], k[4], dc, bt;
-    uint4 vq;
-    if (T > 0) load(0, q, k, vq, dc, bt);
-    for (int t = 0; t < T; ++t) {
-        float qn1[4], kn1[4], dc1 = 0.f, bt1 = 0.f;
-        uint4 vq1 = make_uint4(0, 0, 0, 0);
-        if (t + 1 < T) load(t + 1, qn1, kn1, vq1, dc1, bt1);
-        float kq = 0.0f;
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) kq = __fadd_rn(kq, __fmul_rn(k[ch], q[ch]));
-        kq = warp_sum(kq);
-        const uint32_t vw[4] = {vq.x, vq.y, vq.z, vq.w};
-        float v[kRowsPerWarp];
-#pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r) v[r] = bf((uint16_t)(vw[r >> 1] >> ((r & 1) * 16)));
-        delta_rows(st, q, k, kq, v, dc, bt, y + (int64_t)t * kValDim + hv * kDv + dv0, lane);
-        if (t + 1 < T) {
+    if (n_chunks > 0) issue(0);
+    for (int c = 0; c < n_chunks; ++c) {
+        if (c + 1 < n_chunks) {
+            issue(c + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();  // chunk c is in shared memory for every warp
+        const ScanStage &sg = stage[c & 1];
+        const int t0 = c * kScanChunk;
+        const int n = min(kScanChunk, T - t0);
+        for (int i = 0; i < n; ++i) {
+            float q[4], k[4];
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
-                q[ch] = qn1[ch];
-                k[ch] = kn1[ch];
+                q[ch] = sg.q[i][lane + 32 * ch];
+                k[ch] = sg.k[i][lane + 32 * ch];
             }
-            vq = vq1;
-            dc = dc1;
-            bt = bt1;
+            const uint2 vv = *reinterpret_cast<const uint2 *>(&sg.v[i][warp * kScanRows]);
+            const float v[kScanRows] = {bf((uint16_t)vv.x), bf((uint16_t)(vv.x >> 16)), bf((uint16_t)vv.y),
+                                        bf((uint16_t)(vv.y >> 16))};
+            delta_rows<kScanRows>(st, q, k, sg.kq[i], v, sg.g[i], sg.beta[i],
+                                  y + (int64_t)(t0 + i) * kValDim + hv * kDv + dv0, lane);
         }
+        __syncthreads();  // every warp is done with stage c & 1 before chunk c + 2 refills it
     }
 #pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r)
+    for (int r = 0; r < kScanRows; ++r)
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) st_g[r * kDk + lane + 32 * ch] = st[r][ch];
 }
@@ -340,7 +430,7 @@ __global__ void __launch_bounds__(kWarps * 32) gated_delta_scan_kernel(
 
 size_t gated_delta_prefill_workspace_bytes(int tokens) {
     if (tokens <= 0) return 0;
-    return (size_t)tokens * (2 * kKeyDim + 2 * kHv) * sizeof(float);
+    return (size_t)tokens * (2 * kKeyDim + kHk + 2 * kHv) * sizeof(float);
 }
 
 cudaError_t launch_conv1d_decode(float *states, int64_t num_slots, const int32_t *slots, int batch,
@@ -372,14 +462,23 @@ cudaError_t launch_gated_delta_prefill(float *state, int has_state, const uint16
                                        cudaStream_t stream) {
     float *qn = static_cast<float *>(ws);
     float *kn = qn + (size_t)T * kKeyDim;
-    float *g = kn + (size_t)T * kKeyDim;
+    float *kqn = kn + (size_t)T * kKeyDim;
+    float *g = kqn + (size_t)T * kHk;
     float *beta = g + (size_t)T * kHv;
     cudaError_t e = launch_pdl(gated_delta_prep_kernel, dim3(T, kHk), dim3(128), 0, stream, conv_out, a, b,
-                               a_log, dt_bias, T, qn, kn, g, beta);
+                               a_log, dt_bias, T, qn, kn, kqn, g, beta);
     if (e != cudaSuccess) return e;
-    return launch_pdl(gated_delta_scan_kernel, dim3(kDv / kRowsPerCta, kHv), dim3(kWarps * 32), 0, stream,
-                      state, has_state, conv_out, (const float *)qn, (const float *)kn, (const float *)g,
-                      (const float *)beta, T, y);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(gated_delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    return launch_pdl(gated_delta_scan_kernel, dim3(kDv / kScanRowsPerCta, kHv), dim3(kScanWarps * 32),
+                      kScanSmem, stream, state, has_state, conv_out, (const float *)qn, (const float *)kn,
+                      (const float *)kqn, (const float *)g, (const float *)beta, T, y);
 }
 
 cudaError_t linear_read_error(DevErrorHost *e, bool clear) {
