@@ -506,6 +506,33 @@ int pgc_gated_delta_prefill(float *state, int has_previous_state, const uint16_t
                             const uint16_t *dt_bias, int tokens, uint16_t *y, void *workspace,
                             size_t workspace_bytes, void *stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Context-parallel decode over NVLink peer memory (BASELINE config 5b; the reference is single
+ * device). Rank g of `world` (<= PGC_CP_MAX_RANKS) GPUs holds a contiguous KV shard of one
+ * sequence. pgc_cp_decode_attn runs the split decode over the local shard and then one exchange
+ * kernel that merges the splits, stores the rank's (m, l, o) partial into every rank's exchange
+ * buffer, publishes an epoch flag there, waits (bounded, ~2 s, then PGC_ERR_TIMEOUT through
+ * pgc_device_error) for all ranks' flags and merges the world partials (+ sigmoid gate) into the
+ * bf16 output on every rank. No collective library is involved.
+ * Setup: each rank allocates its buffer with pgc_cp_buffer_alloc, exports it with
+ * pgc_ipc_get_handle, the handles are exchanged by the caller (any host channel) and opened
+ * with pgc_ipc_open_handle; `buffers[i]` is rank i's buffer as mapped in this process (its own
+ * at [rank]). `epoch` starts at 1 and increases by one per call, identically on every rank.
+ * ------------------------------------------------------------------------------------- */
+#define PGC_CP_MAX_RANKS 8
+#define PGC_IPC_HANDLE_BYTES 64
+size_t pgc_cp_buffer_bytes(int world);
+int pgc_cp_buffer_alloc(int world, void **buffer_out);  /* device memory, zeroed */
+int pgc_cp_buffer_free(void *buffer);
+int pgc_ipc_get_handle(void *buffer, void *handle_out);
+int pgc_ipc_open_handle(const void *handle, void **buffer_out);
+int pgc_ipc_close(void *buffer);
+int pgc_cp_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                       int64_t num_pages, const int32_t *block_table, int max_pages,
+                       const int32_t *seq_len, int max_seq_len, float scale, const uint16_t *gate,
+                       uint16_t *out, void *workspace, size_t workspace_bytes,
+                       void *const *buffers, int world, int rank, uint32_t epoch, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

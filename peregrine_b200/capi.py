@@ -124,6 +124,14 @@ SIGNATURES = {
     "pgc_gated_delta_decode": (I32, [P, I64, P, I32, I32, P, P, P, P, P, P, P]),
     "pgc_gated_delta_prefill_workspace_bytes": (SZ, [I32]),
     "pgc_gated_delta_prefill": (I32, [P, I32, P, P, P, P, P, I32, P, P, SZ, P]),
+    "pgc_cp_buffer_bytes": (SZ, [I32]),
+    "pgc_cp_buffer_alloc": (I32, [I32, C.POINTER(P)]),
+    "pgc_cp_buffer_free": (I32, [P]),
+    "pgc_ipc_get_handle": (I32, [P, P]),
+    "pgc_ipc_open_handle": (I32, [P, C.POINTER(P)]),
+    "pgc_ipc_close": (I32, [P]),
+    "pgc_cp_decode_attn": (I32, [P, P, P, I64, P, I32, P, I32, F32, P, P, P, SZ, C.POINTER(P), I32, I32,
+                                 C.c_uint32, P]),
     "pgc_page_pool_create": (P, [I32]),
     "pgc_page_pool_destroy": (None, [P]),
     "pgc_page_pool_alloc": (I32, [P, I32, P]),

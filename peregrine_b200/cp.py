@@ -9,8 +9,9 @@ HBM or latency budget (BASELINE config 5b): rank g holds the contiguous, page-al
   3. pgc_merge_partials: the log-sum-exp combine of attention_decode.metal:215-243 applied to
      the gathered shard partials, optional sigmoid gate, bf16 output on every rank.
 The new token's K/V row is appended only on the rank owning its position (the tail shard).
-The collective runs through torch.distributed (the process-group plumbing); the attention and
-the merge are the library's kernels.
+Two exchange paths: `cp_decode_layer` all-gathers the partials through torch.distributed (NCCL),
+and `PeerExchange.decode_layer` moves them with the library's own exchange kernel over NVLink
+peer memory (merge, stores into every rank's buffer, epoch flags, final merge in one kernel).
 """
 from __future__ import annotations
 
@@ -50,6 +51,65 @@ def gather_partials(local, gathered, group=None) -> None:
     else:
         parts = list(gathered.unbind(0))
         dist.all_gather(parts, local, group=group)
+
+
+class PeerExchange:
+    """Exchange buffers of the context-parallel group, mapped into this process.
+
+    Every rank allocates its buffer in the library (pgc_cp_buffer_alloc), exports a CUDA IPC
+    handle, and the handles travel over the process group as host objects (the only use of
+    torch.distributed here); each rank then maps every peer's buffer. Decode steps then move
+    their partials with the library's exchange kernel, GPU to GPU over NVLink."""
+
+    def __init__(self, world: int, rank: int, group=None):
+        import ctypes as C
+
+        import torch.distributed as dist
+        self.world, self.rank = world, rank
+        own = C.c_void_p()
+        capi.check(capi.lib().pgc_cp_buffer_alloc(world, C.byref(own)), "pgc_cp_buffer_alloc")
+        self._own = own.value
+        handle = (C.c_uint8 * 64)()
+        capi.check(capi.lib().pgc_ipc_get_handle(self._own, handle), "pgc_ipc_get_handle")
+        handles = [None] * world
+        if world > 1:
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        else:
+            handles[0] = bytes(handle)
+        self._opened = []
+        ptrs = []
+        for r in range(world):
+            if r == rank:
+                ptrs.append(self._own)
+                continue
+            h = (C.c_uint8 * 64).from_buffer_copy(handles[r])
+            p = C.c_void_p()
+            capi.check(capi.lib().pgc_ipc_open_handle(h, C.byref(p)), "pgc_ipc_open_handle")
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self.buffers = (C.c_void_p * world)(*ptrs)
+        self.epoch = 0
+
+    def close(self) -> None:
+        for p in self._opened:
+            capi.lib().pgc_ipc_close(p)
+        self._opened = []
+        if self._own:
+            capi.lib().pgc_cp_buffer_free(self._own)
+            self._own = None
+
+    def decode_layer(self, q, k_pages, v_pages, block_table, local_len_dev, local_max_len, scale,
+                     workspace, out, gate=None, stream=None) -> None:
+        """One layer of context-parallel decode for one query token: split decode over the
+        local shard, then the peer exchange + merge kernel; out [16, 256] bf16 on every rank.
+        Every rank calls it once per layer in the same order (the epoch counts calls)."""
+        self.epoch += 1
+        capi.check(capi.lib().pgc_cp_decode_attn(
+            q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), k_pages.shape[0],
+            block_table.data_ptr(), block_table.shape[-1], local_len_dev.data_ptr(),
+            max(local_max_len, 1), scale, None if gate is None else gate.data_ptr(), out.data_ptr(),
+            workspace.data_ptr(), workspace.numel() * workspace.element_size(), self.buffers,
+            self.world, self.rank, self.epoch, capi._stream(stream)), "pgc_cp_decode_attn")
 
 
 def cp_decode_layer(q, k_pages, v_pages, block_table, local_len_dev, local_max_len, scale,

@@ -536,4 +536,82 @@ int pgc_gated_delta_prefill(float *state, int has_previous_state, const uint16_t
                                                   static_cast<cudaStream_t>(stream)));
 }
 
+// ------------------------------------------------------------------ context parallel
+size_t pgc_cp_buffer_bytes(int world) {
+    if (world < 1 || world > PGC_CP_MAX_RANKS) return 0;
+    return cp_buffer_bytes(world);
+}
+
+int pgc_cp_buffer_alloc(int world, void **buffer_out) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (!buffer_out || world < 1 || world > PGC_CP_MAX_RANKS) return PGC_ERR_INVALID;
+    void *p = nullptr;
+    if (cudaMalloc(&p, cp_buffer_bytes(world)) != cudaSuccess) return PGC_ERR_CUDA;
+    if (cudaMemset(p, 0, cp_buffer_bytes(world)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(p);
+        return PGC_ERR_CUDA;
+    }
+    *buffer_out = p;
+    return PGC_OK;
+}
+
+int pgc_cp_buffer_free(void *buffer) {
+    if (!buffer) return PGC_ERR_INVALID;
+    return cuda_status(cudaFree(buffer));
+}
+
+int pgc_ipc_get_handle(void *buffer, void *handle_out) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (!buffer || !handle_out) return PGC_ERR_INVALID;
+    static_assert(sizeof(cudaIpcMemHandle_t) == PGC_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, buffer) != cudaSuccess) return PGC_ERR_CUDA;
+    memcpy(handle_out, &h, sizeof(h));
+    return PGC_OK;
+}
+
+int pgc_ipc_open_handle(const void *handle, void **buffer_out) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (!handle || !buffer_out) return PGC_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void *p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return PGC_ERR_CUDA;
+    *buffer_out = p;
+    return PGC_OK;
+}
+
+int pgc_ipc_close(void *buffer) {
+    if (!buffer) return PGC_ERR_INVALID;
+    return cuda_status(cudaIpcCloseMemHandle(buffer));
+}
+
+int pgc_cp_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                       int64_t num_pages, const int32_t *block_table, int max_pages,
+                       const int32_t *seq_len, int max_seq_len, float scale, const uint16_t *gate,
+                       uint16_t *out, void *workspace, size_t workspace_bytes,
+                       void *const *buffers, int world, int rank, uint32_t epoch, void *stream) {
+    int st = decode_checks(q, k_pages, v_pages, num_pages, block_table, max_pages, seq_len, 1, 1,
+                           max_seq_len, workspace, workspace_bytes);
+    if (st != PGC_OK) return st;
+    if (!out || !buffers || !std::isfinite(scale)) return PGC_ERR_INVALID;
+    if (world < 1 || world > PGC_CP_MAX_RANKS || rank < 0 || rank >= world || epoch == 0)
+        return PGC_ERR_INVALID;
+    float *bufs[PGC_CP_MAX_RANKS] = {};
+    for (int i = 0; i < world; ++i) {
+        if (!buffers[i] || !al16(buffers[i])) return PGC_ERR_INVALID;
+        bufs[i] = static_cast<float *>(buffers[i]);
+    }
+    if (!al16(out) || (gate && !al16(gate))) return PGC_ERR_ALIGN;
+    CUtensorMap tk, tv;
+    if ((st = pool_tensor_map(k_pages, num_pages, &tk)) != PGC_OK) return st;
+    if ((st = pool_tensor_map(v_pages, num_pages, &tv)) != PGC_OK) return st;
+    return cuda_status(launch_cp_decode(q, tk, tv, num_pages, block_table, max_pages, seq_len, max_seq_len,
+                                        scale, gate, out, workspace, bufs, world, rank, epoch,
+                                        current_sm_count(), static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

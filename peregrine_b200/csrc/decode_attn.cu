@@ -570,6 +570,191 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
                       stream, mp);
 }
 
+// ------------------------------------------------------------------------------------------
+// Context-parallel exchange over peer memory (BASELINE config 5b). Rank g holds one contiguous
+// KV shard of a long sequence; the split kernel leaves its per-split partials in the
+// workspace. The exchange kernel (one CTA per row and 32-dim chunk) then (1) LSE-merges those splits into the
+// rank's partial (16 rows x (m, l, o[256])), (2) stores it straight into every rank's exchange
+// buffer over NVLink, (3) publishes an epoch flag in each rank's buffer (release at system
+// scope), (4) waits for every rank's flag in its own buffer (acquire, bounded) and (5) merges the
+// world partials with the gate into the bf16 output. This replaces merge kernel + all-gather + merge kernel:
+// launched right behind the split kernel (programmatic dependent launch), it is resident when
+// the last split finishes. Exchange buffer per rank: [2 parities][world][16][258] f32, then
+// world u32 flags at cp_flags_offset and a u32 CTA counter 128 bytes after them. Parity epoch & 1 double-buffers the slots: rank r cannot
+// start call e + 2 before every rank has published e + 1, which each does only after finishing
+// its reads of call e.
+constexpr int kCpRows = kNumQHeads;
+
+struct CpParams {
+    const float *parts;  // split partials [16][max_splits][258]
+    int max_splits;
+    const int32_t *seq_len;
+    int tokens_per_split;
+    float *bufs[PGC_CP_MAX_RANKS];  // every rank's exchange buffer, as mapped in this process
+    int world, rank;
+    uint32_t epoch;
+    const uint16_t *gate;
+    uint16_t *out;
+};
+
+__device__ __forceinline__ uint32_t *cp_flags(float *buf, int world) {
+    return reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(buf) + cp_flags_offset(world));
+}
+
+// One CTA per (row, 32-dim chunk), 128 CTAs: the 8 warps stride over the local splits (lane =
+// dim), as the merge kernel does, so the L2 reads of up to 256 split partials per row overlap.
+// Each CTA stores its slice of the row partial (chunk 0 also m and l) into every rank's buffer
+// over NVLink, fences at system scope and counts itself in this rank's buffer; the last CTA
+// publishes the epoch flag to every rank. Every CTA then waits for all ranks' flags and merges
+// its slice over the world partials.
+constexpr int kCpCtas = kCpRows * (kHeadDim / 32);
+
+__global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float wm[8], wden[8], wacc[8][32];
+    __shared__ int last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int r = blockIdx.x, d0 = blockIdx.y * 32;
+    const int L = *p.seq_len;
+    int np = L > 0 ? (L + p.tokens_per_split - 1) / p.tokens_per_split : 0;
+    if (np > p.max_splits) np = p.max_splits;
+    const float *base = p.parts + (int64_t)r * p.max_splits * kPartial;
+    float ma = -INFINITY;
+    for (int c = tid; c < np; c += 256) ma = fmaxf(ma, base[(int64_t)c * kPartial]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+    if (lane == 0) wm[warp] = ma;
+    __syncthreads();
+    ma = wm[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) ma = fmaxf(ma, wm[w]);
+    float den = 0.f, acc = 0.f;
+#pragma unroll 4
+    for (int c = warp; c < np; c += 8) {
+        const float *pc = base + (int64_t)c * kPartial;
+        const float mc = pc[0];
+        const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - ma) * kLog2e);
+        den += pc[1] * w;
+        acc += pc[2 + d0 + lane] * w;
+    }
+    if (lane == 0) wden[warp] = den;
+    wacc[warp][lane] = acc;
+    __syncthreads();
+    // this CTA's slice of the rank partial -> every rank's slot [parity][rank][r]
+    const int parity = (int)(p.epoch & 1u);
+    if (warp < p.world) {
+        float *dst = p.bufs[warp] + (((int64_t)parity * p.world + p.rank) * kCpRows + r) * kPartial;
+        float sacc = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sacc += wacc[w][lane];
+        dst[2 + d0 + lane] = sacc;
+        if (blockIdx.y == 0 && lane == 0) {
+            float sden = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) sden += wden[w];
+            dst[0] = ma;
+            dst[1] = sden;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+        unsigned int *count = reinterpret_cast<unsigned int *>(cp_flags(p.bufs[p.rank], p.world) + 32);
+        last = atomicAdd(count, 1u) == (unsigned)(kCpCtas - 1);
+        if (last) {
+            atomicExch(count, 0u);  // ready for the next call
+            __threadfence_system();
+        }
+    }
+    __syncthreads();
+    if (last && tid < p.world) {
+        uint32_t *f = cp_flags(p.bufs[tid], p.world) + p.rank;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(p.epoch) : "memory");
+    }
+    if (tid < p.world) {
+        const uint32_t *f = cp_flags(p.bufs[p.rank], p.world) + tid;
+        const uint64_t t0 = global_timer_ns();
+        for (uint32_t it = 0;; ++it) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if ((int32_t)(v - p.epoch) >= 0) break;
+            if ((it & 63u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
+                record_error(&g_decode_err, kErrWaitTimeout, 1000 + tid);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // merge this slice over the world partials [parity][src][r] of this rank's buffer
+        const float *mine = p.bufs[p.rank] + ((int64_t)parity * p.world * kCpRows + r) * kPartial;
+        const int64_t stride = (int64_t)kCpRows * kPartial;
+        float m2 = -INFINITY;
+        for (int c = 0; c < p.world; ++c) m2 = fmaxf(m2, mine[c * stride]);
+        float d2 = 0.f, a2 = 0.f;
+        for (int c = 0; c < p.world; ++c) {
+            const float *pc = mine + c * stride;
+            const float mc = pc[0];
+            const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - m2) * kLog2e);
+            d2 += pc[1] * w;
+            a2 += pc[2 + d0 + lane] * w;
+        }
+        const int dd = d0 + lane;
+        float v = (d2 == 0.f) ? 0.f : a2 / d2;
+        if (p.gate) {
+            const float g = bf16_bits_to_f32(p.gate[r * kHeadDim + dd]);
+            v = v * (1.0f / (1.0f + expf(-g)));
+        }
+        p.out[r * kHeadDim + dd] = f32_to_bf16_bits(v);
+    }
+}
+
+size_t cp_buffer_bytes(int world) { return cp_flags_offset(world) + 256; }
+
+cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
+                             int64_t num_pages, const int32_t *block_table, int max_pages,
+                             const int32_t *seq_len, int max_seq_len, float scale, const uint16_t *gate,
+                             uint16_t *out, void *workspace, float *const *bufs, int world, int rank,
+                             uint32_t epoch, int sm_count, cudaStream_t stream) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemBytes);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    const DecodePlan plan = decode_plan(1, max_seq_len, sm_count);
+    SplitParams sp;
+    sp.q = q;
+    sp.block_tables = block_table;
+    sp.seq_lens = seq_len;
+    sp.ws = static_cast<float *>(workspace);
+    sp.num_pages = num_pages;
+    sp.max_pages_per_seq = max_pages;
+    sp.num_queries = 1;
+    sp.pages_per_split = plan.pages_per_split;
+    sp.max_splits = plan.max_splits;
+    sp.scale_log2 = scale * kLog2e;
+    cudaError_t e = launch_pdl(decode_split_kernel, dim3(plan.max_splits, kNumKvHeads, 1), dim3(kThreads),
+                               kSmemBytes, stream, tk, tv, sp);
+    if (e != cudaSuccess) return e;
+    CpParams cp;
+    cp.parts = sp.ws;
+    cp.max_splits = plan.max_splits;
+    cp.seq_len = seq_len;
+    cp.tokens_per_split = plan.pages_per_split * kPage;
+    for (int i = 0; i < PGC_CP_MAX_RANKS; ++i) cp.bufs[i] = i < world ? bufs[i] : nullptr;
+    cp.world = world;
+    cp.rank = rank;
+    cp.epoch = epoch;
+    cp.gate = gate;
+    cp.out = out;
+    return launch_pdl(cp_exchange_kernel, dim3(kCpRows, kHeadDim / 32), dim3(256), 0, stream, cp);
+}
+
 cudaError_t decode_read_error(DevErrorHost *e, bool clear) {
     cudaError_t r = cudaMemcpyFromSymbol(e, g_decode_err, sizeof(DevError));
     if (r != cudaSuccess || !clear) return r;

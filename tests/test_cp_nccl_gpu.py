@@ -1,7 +1,9 @@
 """Context-parallel decode on 2 GPUs through the library: each rank holds one KV shard on its
-own GPU, computes pgc_decode_attn_partials, the partials are all-gathered with NCCL and merged
-with pgc_merge_partials; every rank's output must match the oracle over the whole cache within
-the attention tolerance (2e-2 abs + 1e-2 rel). Skipped when fewer than 2 GPUs are visible."""
+own GPU. Two exchange paths: pgc_decode_attn_partials + NCCL all-gather + pgc_merge_partials,
+and pgc_cp_decode_attn, whose exchange kernel stores the partials into the peers' buffers over
+NVLink and waits on epoch flags. Every rank's output must match the oracle over the whole cache
+within the attention tolerance (2e-2 abs + 1e-2 rel). Skipped when fewer than 2 GPUs are
+visible; the peer path runs 5 layers back to back (epoch parity buffers)."""
 import os
 import socket
 
@@ -20,7 +22,7 @@ def _free_port():
     return port
 
 
-def _rank_main(rank, world, port, L, result_dir):
+def _rank_main(rank, world, port, L, result_dir, fused=False):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     import torch
@@ -55,8 +57,21 @@ def _rank_main(rank, world, port, L, result_dir):
         gathered = torch.empty((world, NQ, 258), dtype=torch.float32, device="cuda")
         ws = torch.empty(capi.decode_workspace_bytes(1, 1, max(n, 1)), dtype=torch.uint8, device="cuda")
         out = torch.empty((NQ, D), dtype=torch.int16, device="cuda")
-        cp.cp_decode_layer(dv(q), dv(kp), dv(vp), table, dv(np.array([n], np.int32)), n, 1 / 16,
-                           partial, gathered, ws, out, gate=dv(g))
+        if fused:
+            ex = cp.PeerExchange(world, rank)
+            dist.barrier()
+            # several layers in a row: exercises the epoch parity double buffer
+            for _ in range(5):
+                ex.decode_layer(dv(q), dv(kp), dv(vp), table, dv(np.array([n], np.int32)), n, 1 / 16,
+                                ws, out, gate=dv(g))
+            torch.cuda.synchronize()
+            code, _ = capi.device_error()
+            assert code == 0, code
+            dist.barrier()
+            ex.close()
+        else:
+            cp.cp_decode_layer(dv(q), dv(kp), dv(vp), table, dv(np.array([n], np.int32)), n, 1 / 16,
+                               partial, gathered, ws, out, gate=dv(g))
         torch.cuda.synchronize()
         got = (out.cpu().numpy().view(np.uint16).astype(np.uint32) << 16).view(np.float32)
         kf = np.zeros((L // PAGE + 1, NKV, PAGE, D), np.uint16)
@@ -73,14 +88,15 @@ def _rank_main(rank, world, port, L, result_dir):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("fused", [False, True], ids=["nccl", "peer"])
 @pytest.mark.parametrize("L", [5000, 16])
-def test_cp_decode_two_gpus(tmp_path, L):
+def test_cp_decode_two_gpus(tmp_path, L, fused):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     world = 2
-    mp.start_processes(_rank_main, args=(world, _free_port(), L, str(tmp_path)), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, _free_port(), L, str(tmp_path), fused), nprocs=world,
                        join=True, start_method="spawn")
     for r in range(world):
         ok, err = np.load(tmp_path / f"rank{r}.npy")
