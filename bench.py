@@ -530,6 +530,63 @@ def bench_linear(capi, iters=10):
             "prefill_ms_per_chunk": round(pf_ms, 3)}
 
 
+def bench_q4(capi, iters=20):
+    """The q4 projections of the 8 full-attention layers (q|gate 4096 -> 8192, k and v 4096 ->
+    1024, o 4096 -> 4096; seeded random packed weights): decode of 64 tokens through
+    pgc_q4_linear (bytes = packed weights + scales/biases + activations), and the prefill path
+    of a 1600-token chunk: the weights dequantised once by pgc_q4_dequantize (not timed, as the
+    reference prepares its dense RHS once), then a dense bf16 GEMM (cuBLAS through torch)."""
+    import torch
+    g = torch.Generator(device="cuda")
+    g.manual_seed(9)
+    shapes = [(8192, 4096), (1024, 4096), (1024, 4096), (4096, 4096)]
+    w = [[torch.randint(-2 ** 31, 2 ** 31 - 1, (o, i // 8), dtype=torch.int32, device="cuda", generator=g)
+          for o, i in shapes] for _ in range(LAYERS)]
+    sc = [[(torch.rand((o, i // 64), device="cuda", generator=g) * 0.02).to(torch.bfloat16) for o, i in shapes]
+          for _ in range(LAYERS)]
+    bi = [[(torch.randn((o, i // 64), device="cuda", generator=g) * 0.05).to(torch.bfloat16) for o, i in shapes]
+          for _ in range(LAYERS)]
+    T = 64
+    x = torch.randn((T, 4096), dtype=torch.bfloat16, device="cuda", generator=g)
+    ys = [torch.empty((T, o), dtype=torch.bfloat16, device="cuda") for o, _ in shapes]
+    s = torch.cuda.current_stream()
+
+    def decode_step():
+        st = torch.cuda.current_stream()
+        for l in range(LAYERS):
+            for j in range(4):
+                capi.q4_linear(x, w[l][j], sc[l][j], bi[l][j], ys[j], stream=st)
+
+    # 32 small launches per step: replayed as one CUDA graph, so the figure is device time and
+    # not the Python launch rate
+    decode_step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        decode_step()
+    dec_ms = _ev_time(graph.replay, iters)
+    dec_bytes = LAYERS * sum(o * i // 2 + 2 * (o * i // 64) * 2 + T * (i + o) * 2 for o, i in shapes)
+    dense = [torch.empty((o, i), dtype=torch.bfloat16, device="cuda") for o, i in shapes]
+    for j in range(4):
+        capi.q4_dequantize(w[0][j], sc[0][j], bi[0][j], dense[j], stream=s)
+    Tp = 1600
+    xp = torch.randn((Tp, 4096), dtype=torch.bfloat16, device="cuda", generator=g)
+
+    def prefill_step():
+        for _ in range(LAYERS):
+            for j in range(4):
+                torch.matmul(xp, dense[j].t())
+
+    pf_ms = _ev_time(prefill_step, max(2, iters // 4))
+    flops = LAYERS * sum(2 * Tp * o * i for o, i in shapes)
+    return {"workload": "q4 projections of 8 full-attention layers: decode of 64 tokens (pgc_q4_linear), "
+                        "prefill of a 1600-token chunk (dequantised weights + cuBLAS bf16 GEMM)",
+            "decode_ms_per_step": round(dec_ms, 4), "decode_bytes": dec_bytes,
+            "decode_GB_s": round(dec_bytes / (dec_ms * 1e-3) / 1e9, 1),
+            "prefill_ms_per_chunk": round(pf_ms, 3),
+            "prefill_TFLOP_s": round(flops / (pf_ms * 1e-3) / 1e12, 1)}
+
+
 def bench_config5b(capi, rank, world, iters=20, warmup=3):
     """Config 5b: one 262144-token sequence (8 layers, 16q/4kv, d=256), context-parallel across
     the ranks in contiguous page-aligned KV shards; per layer: q/k RoPE (the new K/V row lands
@@ -781,7 +838,8 @@ def run_ours(args, rank, world, local_rank):
         line["configs"] = {"config5b": cfg5b}
         if world == 1:
             line["configs"].update({"config1": bench_config1(capi), "config2": bench_config2(capi),
-                                    "config3": bench_config3(capi), "linear": bench_linear(capi)})
+                                    "config3": bench_config3(capi), "linear": bench_linear(capi),
+                                    "q4": bench_q4(capi)})
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         gbs, dt, desc = cpu_sample(lens, threads, max_tokens=1 << 30, min_seconds=10.0)
@@ -836,6 +894,7 @@ def main():
         torch.cuda.set_device(local_rank)
         print(json.dumps({"configs": {"config1": bench_config1(capi), "config2": bench_config2(capi),
                                       "config3": bench_config3(capi), "linear": bench_linear(capi),
+                                      "q4": bench_q4(capi),
                                       "config5b": bench_config5b(capi, 0, 1)}}), flush=True)
         return
     try:

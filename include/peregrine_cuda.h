@@ -533,6 +533,24 @@ int pgc_cp_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_
                        uint16_t *out, void *workspace, size_t workspace_bytes,
                        void *const *buffers, int world, int rank, uint32_t epoch, void *stream);
 
+/* ---------------------------------------------------------------------------------------
+ * q4 (group-64 affine) projections around the attention kernels: weight u32 [out][in/8], 8
+ * nibbles per word with the low nibble at the lowest input column; scales and biases bf16
+ * [out][in/64]; w = scale * q + bias (shaders/linear.metal:12-20).
+ * ------------------------------------------------------------------------------------- */
+/* q4_affine_group64_dequantize_bf16 (linear.metal:422-444): out bf16 [out][in], bit-exact
+ * bf16(scale * q + bias). The prefill projections use it once per weight (the reference's
+ * prepared dense RHS, src/model/mlx_nt.zig) followed by a dense bf16 GEMM. in_dim % 64 == 0. */
+int pgc_q4_dequantize(const uint32_t *weight, const uint16_t *scales, const uint16_t *biases,
+                      uint16_t *out, int out_dim, int in_dim, void *stream);
+
+/* linear_q4_affine_group64_qmv_fast_bf16 (linear.metal:158-194) for decode batches:
+ * y[t][o] = sum_k x[t][k] * w[o][k], x [tokens][in] bf16, y [tokens][out] bf16, fp32 sums over
+ * the bf16-rounded dequantised weights. in_dim a multiple of 2048 up to 8192, out_dim % 64 ==
+ * 0; x and weight 16-byte aligned. Best for up to 64 tokens per call (HBM-bound on the packed weights). */
+int pgc_q4_linear(const uint16_t *x, int tokens, const uint32_t *weight, const uint16_t *scales,
+                  const uint16_t *biases, uint16_t *y, int out_dim, int in_dim, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

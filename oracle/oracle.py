@@ -50,6 +50,8 @@ _SIG = {
     "pgo_conv1d_prefill": (None, [P, I32, P, I32, P, P, I32, I32]),
     "pgo_gated_delta_decode": (None, [P, I32, P, P, P, P, P, P]),
     "pgo_gated_delta_prefill": (None, [P, I32, P, P, P, P, P, I32, P]),
+    "pgo_q4_dequantize": (None, [P, P, P, P, I32, I32]),
+    "pgo_q4_linear": (None, [P, P, P, P, P, I32, I32, I32]),
 }
 
 _lib = None
@@ -245,5 +247,22 @@ def gated_delta_prefill(state, has_state, conv_out, a, b, a_log, dt_bias):
     y = np.empty((T, LIN_HV * LIN_DV), np.uint16)
     lib().pgo_gated_delta_prefill(_p(state), int(has_state), _p(conv_out), _p(a), _p(b), _p(a_log),
                                   _p(dt_bias), T, _p(y))
+    return y
+
+
+# ------------------------------------------------------------------ q4 projections (pgo_linear.c)
+def q4_dequantize(w, scales, biases):
+    """w u32 [out][in/8], scales/biases bf16 [out][in/64] -> bf16 [out][in]."""
+    out_dim, in_dim = w.shape[0], w.shape[1] * 8
+    out = np.empty((out_dim, in_dim), np.uint16)
+    lib().pgo_q4_dequantize(_p(w), _p(scales), _p(biases), _p(out), out_dim, in_dim)
+    return out
+
+
+def q4_linear(x, w, scales, biases):
+    """x bf16 [T][in] -> y bf16 [T][out]."""
+    T, out_dim, in_dim = x.shape[0], w.shape[0], w.shape[1] * 8
+    y = np.empty((T, out_dim), np.uint16)
+    lib().pgo_q4_linear(_p(x), _p(w), _p(scales), _p(biases), _p(y), T, out_dim, in_dim)
     return y
 

@@ -2,6 +2,8 @@
  * pgo_linear.c — CPU ORACLE (test infrastructure only) for the linear-attention (Gated-DeltaNet)
  * state producers: the depthwise causal conv1d + SiLU and the gated delta-rule recurrence.
  *
+ * Also the q4 (group-64 affine) projections around the attention kernels.
+ *
  * Scalar restatement of the reference shaders, each function citing the file:line it follows
  * (paths within XiaoConstantine/peregrine). Shapes are the model's (src/model/block_linear.zig:
  * 18-26): Hk = 16 key heads, Hv = 32 value heads, Dk = Dv = 128, conv_dim = 2*Hk*Dk + Hv*Dv =
@@ -15,6 +17,7 @@
 #include "pgo_oracle.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #define LHK 16
@@ -210,6 +213,53 @@ void pgo_gated_delta_prefill(float *state, int has_state, const uint16_t *conv_o
             gates(a + (size_t)t * LHV, b + (size_t)t * LHV, A_log, dt_bias, hv, &decay, &beta);
             delta_token(state + (size_t)hv * LDV * LDK, q[hk], k[hk], row + 2 * LKEY + hv * LDV, decay,
                         beta, y + (size_t)t * LVAL + hv * LDV);
+        }
+    }
+}
+
+/* ---------------------------------------------------------------- q4 projections
+ * Format of shaders/linear.metal:12-20: weight u32 [out][in/8] (8 nibbles, low nibble = lowest
+ * column), scales and biases bf16 [out][in/64]; w = scale * q + bias. */
+
+/* q4_affine_group64_dequantize_bf16 (linear.metal:422-444): bf16(scale * q + bias), the product
+ * and the sum each rounded to fp32. */
+void pgo_q4_dequantize(const uint32_t *w, const uint16_t *scales, const uint16_t *biases,
+                       uint16_t *out, int out_dim, int in_dim) {
+    const int words = in_dim / 8, groups = in_dim / 64;
+    for (int o = 0; o < out_dim; ++o)
+        for (int k = 0; k < in_dim; ++k) {
+            const uint32_t q = (w[(size_t)o * words + k / 8] >> ((k & 7) * 4)) & 0xFu;
+            const float s = pgo_bf16_to_f32(scales[(size_t)o * groups + k / 64]);
+            const float b = pgo_bf16_to_f32(biases[(size_t)o * groups + k / 64]);
+            const float p = s * (float)q;
+            out[(size_t)o * in_dim + k] = pgo_f32_to_bf16(p + b);
+        }
+}
+
+/* The decode projection of linear.metal:64-123 (q4_affine_group64_qmv_fast_compute4_bf16): per
+ * 64-input group g of row o, y += scale * sum_k(q_k * x_k) + bias * sum_k(x_k), everything in
+ * fp32 (the weights are never rounded to bf16 on this path), then one bf16 rounding of y. Sums
+ * run in k order. x [T][in] bf16, y [T][out] bf16. */
+void pgo_q4_linear(const uint16_t *x, const uint32_t *w, const uint16_t *scales, const uint16_t *biases,
+                   uint16_t *y, int T, int out_dim, int in_dim) {
+    const int words = in_dim / 8, groups = in_dim / 64;
+    for (int t = 0; t < T; ++t) {
+        const uint16_t *xr = x + (size_t)t * in_dim;
+        for (int o = 0; o < out_dim; ++o) {
+            float acc = 0.0f;
+            for (int g = 0; g < groups; ++g) {
+                float qx = 0.0f, xs = 0.0f;
+                for (int k = g * 64; k < g * 64 + 64; ++k) {
+                    const uint32_t q = (w[(size_t)o * words + k / 8] >> ((k & 7) * 4)) & 0xFu;
+                    const float xv = pgo_bf16_to_f32(xr[k]);
+                    qx += (float)q * xv;
+                    xs += xv;
+                }
+                const float sc = pgo_bf16_to_f32(scales[(size_t)o * groups + g]);
+                const float bi = pgo_bf16_to_f32(biases[(size_t)o * groups + g]);
+                acc += sc * qx + bi * xs;
+            }
+            y[(size_t)t * out_dim + o] = pgo_f32_to_bf16(acc);
         }
     }
 }

@@ -118,6 +118,12 @@ void pgo_gated_delta_prefill(float *state, int has_state, const uint16_t *conv_o
                              const uint16_t *b, const float *A_log, const uint16_t *dt_bias, int T,
                              uint16_t *y);
 
+/* q4 group-64 affine projections (pgo_linear.c). */
+void pgo_q4_dequantize(const uint32_t *w, const uint16_t *scales, const uint16_t *biases,
+                       uint16_t *out, int out_dim, int in_dim);
+void pgo_q4_linear(const uint16_t *x, const uint32_t *w, const uint16_t *scales, const uint16_t *biases,
+                   uint16_t *y, int T, int out_dim, int in_dim);
+
 #ifdef __cplusplus
 }
 #endif

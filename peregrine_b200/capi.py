@@ -132,6 +132,8 @@ SIGNATURES = {
     "pgc_ipc_close": (I32, [P]),
     "pgc_cp_decode_attn": (I32, [P, P, P, I64, P, I32, P, I32, F32, P, P, P, SZ, C.POINTER(P), I32, I32,
                                  C.c_uint32, P]),
+    "pgc_q4_dequantize": (I32, [P, P, P, P, I32, I32, P]),
+    "pgc_q4_linear": (I32, [P, I32, P, P, P, P, I32, I32, P]),
     "pgc_page_pool_create": (P, [I32]),
     "pgc_page_pool_destroy": (None, [P]),
     "pgc_page_pool_alloc": (I32, [P, I32, P]),
@@ -424,4 +426,17 @@ def gated_delta_prefill(state, has_previous_state, conv_out, a, b, a_log, dt_bia
                                         _ptr(b), _ptr(a_log), _ptr(dt_bias), conv_out.shape[0], _ptr(y),
                                         _ptr(workspace), workspace.numel() * workspace.element_size(),
                                         _stream(stream)), "pgc_gated_delta_prefill")
+
+
+# ----------------------------------------------------------------------------- q4 projections
+def q4_dequantize(weight, scales, biases, out, stream=None) -> None:
+    """weight int32/uint32 [out][in/8], scales/biases bf16 [out][in/64] -> out bf16 [out][in]."""
+    check(lib().pgc_q4_dequantize(_ptr(weight), _ptr(scales), _ptr(biases), _ptr(out), out.shape[0],
+                                  out.shape[1], _stream(stream)), "pgc_q4_dequantize")
+
+
+def q4_linear(x, weight, scales, biases, y, stream=None) -> None:
+    """x bf16 [tokens][in] -> y bf16 [tokens][out]."""
+    check(lib().pgc_q4_linear(_ptr(x), x.shape[0], _ptr(weight), _ptr(scales), _ptr(biases), _ptr(y),
+                              y.shape[1], x.shape[1], _stream(stream)), "pgc_q4_linear")
 

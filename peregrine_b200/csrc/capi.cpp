@@ -614,4 +614,33 @@ int pgc_cp_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_
                                         current_sm_count(), static_cast<cudaStream_t>(stream)));
 }
 
+// ------------------------------------------------------------------ q4 projections
+int pgc_q4_dequantize(const uint32_t *weight, const uint16_t *scales, const uint16_t *biases,
+                      uint16_t *out, int out_dim, int in_dim, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (out_dim < 0 || in_dim <= 0 || in_dim % 64 != 0) return PGC_ERR_INVALID;
+    if (out_dim == 0) return PGC_OK;
+    if (!weight || !scales || !biases || !out) return PGC_ERR_INVALID;
+    if (!al16(out) || ((uintptr_t)weight & 3u) != 0) return PGC_ERR_ALIGN;
+    return cuda_status(launch_q4_dequantize(weight, scales, biases, out, out_dim, in_dim,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_q4_linear(const uint16_t *x, int tokens, const uint32_t *weight, const uint16_t *scales,
+                  const uint16_t *biases, uint16_t *y, int out_dim, int in_dim, void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (tokens < 0 || out_dim <= 0 || in_dim <= 0) return PGC_ERR_INVALID;
+    // 8 K slices of whole 64-input groups, a multiple of 4 groups each (8-byte metadata copies)
+    if (in_dim % 2048 != 0 || in_dim > 8192 || out_dim % 64 != 0) return PGC_ERR_INVALID;
+    if (tokens == 0) return PGC_OK;
+    if (!x || !weight || !scales || !biases || !y) return PGC_ERR_INVALID;
+    if (!al16(x) || !al16(weight) || ((uintptr_t)scales & 7u) != 0 || ((uintptr_t)biases & 7u) != 0 ||
+        ((uintptr_t)y & 3u) != 0)
+        return PGC_ERR_ALIGN;
+    return cuda_status(launch_q4_linear(x, tokens, weight, scales, biases, y, out_dim, in_dim,
+                                        static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

@@ -107,4 +107,11 @@ cudaError_t launch_gated_delta_prefill(float *state, int has_state, const uint16
                                        cudaStream_t stream);
 cudaError_t linear_read_error(DevErrorHost *e, bool clear);
 
+// q4_linear.cu
+cudaError_t launch_q4_dequantize(const uint32_t *w, const uint16_t *scales, const uint16_t *biases,
+                                 uint16_t *out, int out_dim, int in_dim, cudaStream_t stream);
+cudaError_t launch_q4_linear(const uint16_t *x, int T, const uint32_t *w, const uint16_t *scales,
+                             const uint16_t *biases, uint16_t *y, int out_dim, int in_dim,
+                             cudaStream_t stream);
+
 }  // namespace pgc
