@@ -269,15 +269,15 @@ __global__ void __launch_bounds__(kWarps * 32) gated_delta_decode_kernel(
 
 // qk_l2norm_prefill_bf16 (gated_norm.metal:191-245) and gating_many_bf16 (:247-263) for one
 // sequence: block (token, key head) of 128 threads with the same shared-memory tree. Outputs are
-// head-major so that the scan stages a chunk of tokens with contiguous copies: q, k f32
-// [16][T][128]; kq f32 [16][T] (q.k of the normalised vectors, lane-chunk order then the warp
-// butterfly, as the scan would form it); g, beta f32 [32][T] (value heads 2hk and 2hk+1).
+// head-major so that a chunk of tokens is contiguous: q, k f32 [16][T][128]; the log of the
+// decay (-exp(A_log) * softplus(a + dt_bias), whose exp is gating_many's g) and beta f32
+// [32][T] for value heads 2hk and 2hk+1.
 __global__ void __launch_bounds__(128) gated_delta_prep_kernel(const uint16_t *conv_out,
                                                                const uint16_t *a, const uint16_t *b,
                                                                const float *a_log,
                                                                const uint16_t *dt_bias, int T,
-                                                               float *qn, float *kn, float *kqn,
-                                                               float *g, float *beta) {
+                                                               float *qn, float *kn, float *lgd,
+                                                               float *beta) {
     pdl_trigger();
     pdl_wait();
     __shared__ float pq[128], pk[128];
@@ -298,139 +298,382 @@ __global__ void __launch_bounds__(128) gated_delta_prep_kernel(const uint16_t *c
     const float q_inv = inv_sqrt(__fadd_rn(pq[0], 1.0e-6f));
     const float k_inv = inv_sqrt(__fadd_rn(pk[0], 1.0e-6f));
     const float q_scale = inv_sqrt((float)kDk);
-    const float qo = __fmul_rn(__fmul_rn(qv, q_inv), q_scale);
-    const float ko = __fmul_rn(kv, k_inv);
     const int64_t o = ((int64_t)hk * T + t) * kDk + tid;
-    qn[o] = qo;
-    kn[o] = ko;
-    __syncthreads();  // the tree is done with pq: reuse it for q.k
-    pq[tid] = __fmul_rn(ko, qo);
-    __syncthreads();
-    if (tid < 32) {
-        float sacc = 0.0f;
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) sacc = __fadd_rn(sacc, pq[tid + 32 * ch]);
-        sacc = warp_sum(sacc);
-        if (tid == 0) kqn[(int64_t)hk * T + t] = sacc;
-        if (tid < 2) {
-            const int hv = 2 * hk + tid;
-            float d, bt;
-            gates(bf(a[(int64_t)t * kHv + hv]), bf(dt_bias[hv]), a_log[hv], bf(b[(int64_t)t * kHv + hv]), &d, &bt);
-            g[(int64_t)hv * T + t] = d;
-            beta[(int64_t)hv * T + t] = bt;
-        }
+    qn[o] = __fmul_rn(__fmul_rn(qv, q_inv), q_scale);
+    kn[o] = __fmul_rn(kv, k_inv);
+    if (tid < 2) {
+        const int hv = 2 * hk + tid;
+        const float x = __fadd_rn(bf(a[(int64_t)t * kHv + hv]), bf(dt_bias[hv]));
+        const float sp = __fadd_rn(fmaxf(x, 0.0f), logf(__fadd_rn(1.0f, expf(-fabsf(x)))));
+        lgd[(int64_t)hv * T + t] = __fmul_rn(-expf(a_log[hv]), sp);
+        beta[(int64_t)hv * T + t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-bf(b[(int64_t)t * kHv + hv]))));
     }
 }
 
-// gated_delta_prefill_h128_norm_prepared_value_major_r8_bf16 (gated_delta.metal:35-138): the
-// scan over T tokens of one sequence, state rows in registers. The token loop is sequential, so
-// what bounds it is the latency of one token's update; the inputs every warp of a head needs
-// (q, k, q.k, gates) are staged once per CTA in shared memory, 64 tokens at a time and double
-// buffered with cp.async, instead of being re-read from L2 by each warp. CTA = 32 value rows of
-// one head (8 warps x 4 rows); grid 4 x 32 = 128 CTAs, one per SM: per token each SM issues the
-// ~180 instructions of each of its 8 warps, and more rows per SM would make issue the bound.
-constexpr int kScanRows = 4;
-constexpr int kScanWarps = 8;
-constexpr int kScanRowsPerCta = kScanRows * kScanWarps;
-constexpr int kScanChunk = 64;
-struct ScanStage {
-    float q[kScanChunk][kDk];
-    float k[kScanChunk][kDk];
-    float kq[kScanChunk];
-    float g[kScanChunk];
-    float beta[kScanChunk];
-    uint16_t v[kScanChunk][kScanRowsPerCta];
+// ---------------------------------------------------------------- chunked recurrence
+// The prefill recurrence over T tokens in chunks of C = 64, the standard chunked form of the
+// gated delta rule. Within a chunk, with lg_i the cumulative log-decay from the chunk start
+// (log space, so products of decays cannot underflow) and S_0 the state entering the chunk:
+//   delta = T_c (beta * (V - e^{lg} * (K S_0^T))),  T_c = (I + A)^{-1},
+//   A_ij = beta_i e^{lg_i - lg_j} (k_i . k_j) for j < i,
+// so with U = T_c (beta * V) and W = T_c (beta * e^{lg} * K) (no state in either):
+//   delta = U - W S_0^T
+//   y     = e^{lg} * (Q S_0^T) + QKm delta,   QKm_ij = e^{lg_i - lg_j} (q_i . k_j) for j <= i
+//   S_C   = e^{lg_C} S_0 + delta^T (e^{lg_C - lg} * K).
+// This is the sequential recurrence of gated_delta.metal:35-138 regrouped: the same fp32
+// arithmetic in a different order. gated_delta_chunk_kernel computes U, W, QKm and lg for every
+// (chunk, value head) in parallel; gated_delta_chunk_scan_kernel then walks the chunks with the
+// state, each CTA owning 32 value rows of one head (the rows are independent given K, beta, g).
+constexpr int kChunk = 64;
+constexpr int kRowP = kDk + 4;      // f32 rows of 128 padded by 16 B: float4 rows 4 banks apart
+constexpr int kQKP = kChunk + 4;    // f32 rows of 64, same padding
+
+struct ChunkWs {
+    // per (value head, chunk): U, W [64][128], QKm [64][64], lg [64]
+    static constexpr int64_t kUW = (int64_t)kChunk * kDk;
+    static constexpr int64_t kQK = (int64_t)kChunk * kChunk;
+    static constexpr int64_t kPer = 2 * kUW + kQK + kChunk;
 };
-constexpr int kScanSmem = 2 * (int)sizeof(ScanStage);
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async4(void *smem_dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
+// 16-byte copy that writes zeros without reading when `valid` is false
+__device__ __forceinline__ void cp_async16_zfill(void *smem_dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ void fma4(float (&acc)[4], float a, const float4 &b) {
+    acc[0] = fmaf(a, b.x, acc[0]);
+    acc[1] = fmaf(a, b.y, acc[1]);
+    acc[2] = fmaf(a, b.z, acc[2]);
+    acc[3] = fmaf(a, b.w, acc[3]);
+}
+__device__ __forceinline__ float dot4(const float4 &a, const float4 &b, float acc) {
+    acc = fmaf(a.x, b.x, acc);
+    acc = fmaf(a.y, b.y, acc);
+    acc = fmaf(a.z, b.z, acc);
+    return fmaf(a.w, b.w, acc);
 }
 
-__global__ void __launch_bounds__(kScanWarps * 32) gated_delta_scan_kernel(
-    float *state, int has_state, const uint16_t *conv_out, const float *qn, const float *kn,
-    const float *kqn, const float *g, const float *beta, int T, uint16_t *y) {
+// Per (chunk, value head): A, QKm, then U and W by forward substitution. 256 threads.
+// Shared memory (~101 KB, two CTAs per SM): K, Q [64][132] (later the U and W solutions
+// [64][128] each), A transposed At[j][i] [64][68], lg, beta [64], the V slice [64][128] bf16.
+constexpr int kChunkSmemFloats = 2 * kChunk * kRowP + kChunk * kQKP + 2 * kChunk + kChunk * kDv / 2;
+__global__ void __launch_bounds__(256, 2) gated_delta_chunk_kernel(const float *qn, const float *kn,
+                                                                const float *lgd, const float *beta,
+                                                                const uint16_t *conv_out, int T,
+                                                                float *cw) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ __align__(16) uint8_t scan_smem[];
-    ScanStage *stage = reinterpret_cast<ScanStage *>(scan_smem);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
-    const int hv = blockIdx.y;
+    extern __shared__ __align__(16) float ck_smem[];
+    float *Ks = ck_smem;                 // [64][132]
+    float *Qs = Ks + kChunk * kRowP;     // [64][132]
+    float *At = Qs + kChunk * kRowP;     // [64][68]: At[j][i] = A[i][j]
+    float *lg = At + kChunk * kQKP;      // [64]
+    float *bt = lg + kChunk;             // [64]
+    uint16_t *vst = reinterpret_cast<uint16_t *>(bt + kChunk);  // [64][128] bf16
+    const int c = blockIdx.x, hv = blockIdx.y, tid = threadIdx.x;
     const int hk = hv / (kHv / kHk);
-    const int row0 = blockIdx.x * kScanRowsPerCta;
-    const int dv0 = row0 + warp * kScanRows;
-    float *st_g = state + ((int64_t)hv * kDv + dv0) * kDk;
-    float st[kScanRows][4];
-#pragma unroll
-    for (int r = 0; r < kScanRows; ++r)
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) st[r][ch] = has_state ? st_g[r * kDk + lane + 32 * ch] : 0.0f;
-
-    const int n_chunks = (T + kScanChunk - 1) / kScanChunk;
-    auto issue = [&](int c) {
-        ScanStage &sg = stage[c & 1];
-        const int t0 = c * kScanChunk;
-        const int n = min(kScanChunk, T - t0);
-        const float *qs = qn + ((int64_t)hk * T + t0) * kDk;
-        const float *ks = kn + ((int64_t)hk * T + t0) * kDk;
-        for (int i = tid; i < n * (kDk / 4); i += kScanWarps * 32) {
-            cp_async16(&sg.q[0][0] + 4 * i, qs + 4 * i);
-            cp_async16(&sg.k[0][0] + 4 * i, ks + 4 * i);
+    const int nc = gridDim.x;
+    const int t0 = c * kChunk;
+    const int n = min(kChunk, T - t0);
+    {
+        const float *ksrc = kn + ((int64_t)hk * T + t0) * kDk;
+        const float *qsrc = qn + ((int64_t)hk * T + t0) * kDk;
+        for (int i = tid; i < kChunk * kDk / 4; i += 256) {
+            const int r = i / (kDk / 4), k4 = i % (kDk / 4);
+            const bool ok = r < n;
+            cp_async16_zfill(Ks + r * kRowP + 4 * k4, ok ? ksrc + r * kDk + 4 * k4 : ksrc, ok);
+            cp_async16_zfill(Qs + r * kRowP + 4 * k4, ok ? qsrc + r * kDk + 4 * k4 : qsrc, ok);
         }
-        for (int i = tid; i < n; i += kScanWarps * 32) {
-            cp_async4(&sg.kq[i], kqn + (int64_t)hk * T + t0 + i);
-            cp_async4(&sg.g[i], g + (int64_t)hv * T + t0 + i);
-            cp_async4(&sg.beta[i], beta + (int64_t)hv * T + t0 + i);
-        }
-        // v: this CTA's 64 rows of each token = 128 contiguous bytes of conv_out
-        for (int i = tid; i < n * (kScanRowsPerCta / 8); i += kScanWarps * 32) {
-            const int tt = i / (kScanRowsPerCta / 8), u = i % (kScanRowsPerCta / 8);
-            cp_async16(&sg.v[tt][8 * u],
-                       conv_out + (int64_t)(t0 + tt) * kConv + 2 * kKeyDim + hv * kDv + row0 + 8 * u);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    if (n_chunks > 0) issue(0);
-    for (int c = 0; c < n_chunks; ++c) {
-        if (c + 1 < n_chunks) {
-            issue(c + 1);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
-        __syncthreads();  // chunk c is in shared memory for every warp
-        const ScanStage &sg = stage[c & 1];
-        const int t0 = c * kScanChunk;
-        const int n = min(kScanChunk, T - t0);
-        for (int i = 0; i < n; ++i) {
-            float q[4], k[4];
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                q[ch] = sg.q[i][lane + 32 * ch];
-                k[ch] = sg.k[i][lane + 32 * ch];
-            }
-            const uint2 vv = *reinterpret_cast<const uint2 *>(&sg.v[i][warp * kScanRows]);
-            const float v[kScanRows] = {bf((uint16_t)vv.x), bf((uint16_t)(vv.x >> 16)), bf((uint16_t)vv.y),
-                                        bf((uint16_t)(vv.y >> 16))};
-            delta_rows<kScanRows>(st, q, k, sg.kq[i], v, sg.g[i], sg.beta[i],
-                                  y + (int64_t)(t0 + i) * kValDim + hv * kDv + dv0, lane);
-        }
-        __syncthreads();  // every warp is done with stage c & 1 before chunk c + 2 refills it
+        cp_async_commit();
     }
+    // beta and the per-token log decays (the decays go through `lg` first, then each of the 64
+    // threads sums its own prefix in token order, the same order as one running sum)
+    if (tid < kChunk) {
+        bt[tid] = tid < n ? beta[(int64_t)hv * T + t0 + tid] : 0.f;
+        lg[tid] = tid < n ? lgd[(int64_t)hv * T + t0 + tid] : 0.f;
+    }
+    // V slice of the chunk (bf16), coalesced
+    for (int i = tid; i < kChunk * kDv; i += 256) {
+        const int r = i / kDv, k = i % kDv;
+        vst[i] = r < n ? conv_out[(int64_t)(t0 + r) * kConv + 2 * kKeyDim + hv * kDv + k] : 0;
+    }
+    __syncthreads();
+    float lgi = 0.f;
+    if (tid < kChunk)
+        for (int j = 0; j <= tid; ++j) lgi += lg[j];
+    __syncthreads();
+    if (tid < kChunk) lg[tid] = lgi;
+    cp_async_wait<0>();
+    __syncthreads();
+    float *out = cw + ((int64_t)hv * nc + c) * ChunkWs::kPer;
+    float *U = out, *W = out + ChunkWs::kUW, *QK = out + 2 * ChunkWs::kUW, *LG = QK + ChunkWs::kQK;
+    // A (strictly lower) and QKm (lower incl. diagonal): 4x4 (i, j) per thread, i = bi + 16 ii,
+    // j = bj + 16 jj, dot products over k in order k = 0..127.
+    {
+        const int bi = tid >> 4, bj = tid & 15;
+        float kk[4][4] = {}, qk[4][4] = {};
+#pragma unroll 2
+        for (int k = 0; k < kDk; k += 4) {
+            float4 ki[4], qi[4], kj[4];
 #pragma unroll
-    for (int r = 0; r < kScanRows; ++r)
+            for (int x = 0; x < 4; ++x) {
+                ki[x] = ld4(Ks + (bi + 16 * x) * kRowP + k);
+                qi[x] = ld4(Qs + (bi + 16 * x) * kRowP + k);
+                kj[x] = ld4(Ks + (bj + 16 * x) * kRowP + k);
+            }
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) st_g[r * kDk + lane + 32 * ch] = st[r][ch];
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) {
+                    kk[x][y] = dot4(ki[x], kj[y], kk[x][y]);
+                    qk[x][y] = dot4(qi[x], kj[y], qk[x][y]);
+                }
+        }
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                const int i = bi + 16 * x, j = bj + 16 * y;
+                const bool in = j <= i && i < n;
+                const float dec = in ? expf(lg[i] - lg[j]) : 0.f;
+                At[j * kQKP + i] = j < i ? bt[i] * dec * kk[x][y] : 0.f;
+                QK[i * kChunk + j] = dec * qk[x][y];
+            }
+    }
+    if (tid < kChunk) LG[tid] = lg[tid];
+    // right-hand sides: column `col` of beta * V (threads 0-127) or beta * e^{lg} * K (128-255)
+    const int col = tid & 127;
+    const bool is_w = tid >= 128;
+    float *us = is_w ? Qs : Ks;  // [64][128], free once the right-hand sides are in registers
+    float rhs[kChunk];
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i)
+        rhs[i] = is_w ? bt[i] * expf(lg[i]) * Ks[i * kRowP + col] : bt[i] * bf(vst[i * kDv + col]);
+    __syncthreads();  // At complete; every thread has read K and Q
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) us[i * kDk + col] = rhs[i];
+    // forward substitution u_i = r_i - sum_{j<i} A_ij u_j in 16-row blocks: the earlier blocks
+    // enter as independent dot products, then a 16-step solve inside the block. Each thread
+    // touches only its own column of `us`.
+    for (int blk = 0; blk < kChunk / 16; ++blk) {
+        float r[16];
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) r[ii] = us[(blk * 16 + ii) * kDk + col];
+        for (int j = 0; j < blk * 16; ++j) {
+            const float uj = us[j * kDk + col];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 a = ld4(At + j * kQKP + blk * 16 + 4 * q);
+                r[4 * q + 0] = fmaf(-a.x, uj, r[4 * q + 0]);
+                r[4 * q + 1] = fmaf(-a.y, uj, r[4 * q + 1]);
+                r[4 * q + 2] = fmaf(-a.z, uj, r[4 * q + 2]);
+                r[4 * q + 3] = fmaf(-a.w, uj, r[4 * q + 3]);
+            }
+        }
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+#pragma unroll
+            for (int ii = jj + 1; ii < 16; ++ii)
+                r[ii] = fmaf(-At[(blk * 16 + jj) * kQKP + blk * 16 + ii], r[jj], r[ii]);
+        }
+#pragma unroll
+        for (int ii = 0; ii < 16; ++ii) us[(blk * 16 + ii) * kDk + col] = r[ii];
+    }
+    float *dst = is_w ? W : U;
+    for (int i = 0; i < kChunk; ++i) dst[i * kDk + col] = us[i * kDk + col];
+}
+
+// The state walk: CTA = (32 value rows, value head), 256 threads; the 32 x 128 state slice stays
+// in shared memory across chunks. Each chunk's tiles are staged in shared memory with cp.async
+// in two groups, A = {W, Q, U slice} and B = {K, QKm, lg}: A of chunk c+1 loads during phase 2
+// of chunk c (after phase 1 has released W, Q, U), B of chunk c+1 during phase 1 of chunk c+1.
+//   phase 1   delta = U - W S^T, QS = Q S^T       thread: rows i = 2ty, 2ty+1; value rows tx + 8m
+//   phase 2a  y = e^{lg} QS + QKm delta           same mapping, from registers
+//   phase 2b  S = e^{lg_C} S + (e^{lg_C - lg} delta)^T K   thread: value rows 4tx.., keys 4ty..
+constexpr int kRowsScan = 32;
+constexpr int kDP = kRowsScan + 4;
+struct ScanSmem {
+    static constexpr int S = 0;                              // [32][132]
+    static constexpr int W = S + kRowsScan * kRowP;          // [64][132]
+    static constexpr int Q = W + kChunk * kRowP;             // [64][132]
+    static constexpr int U = Q + kChunk * kRowP;             // [64][32]
+    static constexpr int K = U + kChunk * kRowsScan;         // [64][128]
+    static constexpr int QK = K + kChunk * kDk;              // [64][68]
+    static constexpr int LG = QK + kChunk * kQKP;            // [64]
+    static constexpr int D = LG + kChunk;                    // [64][36]
+    static constexpr int Ds = D + kChunk * kDP;              // [64][36], scaled by e^{lg_C - lg}
+    static constexpr int kFloats = Ds + kChunk * kDP;
+};
+
+__global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *state, int has_state,
+                                                                     const float *qn, const float *kn,
+                                                                     const float *cw, int T,
+                                                                     uint16_t *y) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) float cs_smem[];
+    float *S = cs_smem + ScanSmem::S, *Ws = cs_smem + ScanSmem::W, *Qs = cs_smem + ScanSmem::Q;
+    float *Us = cs_smem + ScanSmem::U, *Ks = cs_smem + ScanSmem::K, *QKs = cs_smem + ScanSmem::QK;
+    float *LGs = cs_smem + ScanSmem::LG, *Dl = cs_smem + ScanSmem::D, *Dsc = cs_smem + ScanSmem::Ds;
+    const int tid = threadIdx.x, tx = tid & 7, ty = tid >> 3;
+    const int hv = blockIdx.y, hk = hv / (kHv / kHk);
+    const int r0 = blockIdx.x * kRowsScan;
+    const int nc = (T + kChunk - 1) / kChunk;
+    float *st_g = state + ((int64_t)hv * kDv + r0) * kDk;
+
+    auto issue_a = [&](int c) {
+        const int t0 = c * kChunk, n = min(kChunk, T - t0);
+        const float *base = cw + ((int64_t)hv * nc + c) * ChunkWs::kPer;
+        const float *Wg = base + ChunkWs::kUW;
+        const float *Qg = qn + ((int64_t)hk * T + t0) * kDk;
+        for (int i = tid; i < kChunk * kDk / 4; i += 256) {
+            const int r = i >> 5, k4 = i & 31;
+            cp_async16(Ws + r * kRowP + 4 * k4, Wg + r * kDk + 4 * k4);
+            const bool ok = r < n;
+            cp_async16_zfill(Qs + r * kRowP + 4 * k4, ok ? Qg + r * kDk + 4 * k4 : Qg, ok);
+        }
+        for (int i = tid; i < kChunk * kRowsScan / 4; i += 256) {
+            const int r = i >> 3, q = i & 7;
+            cp_async16(Us + r * kRowsScan + 4 * q, base + r * kDk + r0 + 4 * q);
+        }
+        cp_async_commit();
+    };
+    auto issue_b = [&](int c) {
+        const int t0 = c * kChunk, n = min(kChunk, T - t0);
+        const float *base = cw + ((int64_t)hv * nc + c) * ChunkWs::kPer;
+        const float *QKg = base + 2 * ChunkWs::kUW;
+        const float *Kg = kn + ((int64_t)hk * T + t0) * kDk;
+        for (int i = tid; i < kChunk * kDk / 4; i += 256) {
+            const int r = i >> 5, k4 = i & 31;
+            const bool ok = r < n;
+            cp_async16_zfill(Ks + r * kDk + 4 * k4, ok ? Kg + r * kDk + 4 * k4 : Kg, ok);
+        }
+        for (int i = tid; i < kChunk * kChunk / 4; i += 256) {
+            const int r = i >> 4, q = i & 15;
+            cp_async16(QKs + r * kQKP + 4 * q, QKg + r * kChunk + 4 * q);
+        }
+        if (tid < kChunk / 4) cp_async16(LGs + 4 * tid, QKg + ChunkWs::kQK + 4 * tid);
+        cp_async_commit();
+    };
+
+    issue_a(0);
+    issue_b(0);
+    for (int i = tid; i < kRowsScan * kDk; i += 256)
+        S[(i / kDk) * kRowP + i % kDk] = has_state ? st_g[i] : 0.f;
+    for (int c = 0; c < nc; ++c) {
+        const int t0 = c * kChunk, n = min(kChunk, T - t0);
+        cp_async_wait<1>();  // A(c) landed (B(c) may still be in flight)
+        __syncthreads();
+        // phase 1
+        float d[2][4] = {}, qs[2][4] = {};
+        {
+            const float *w0 = Ws + (2 * ty) * kRowP, *w1 = w0 + kRowP;
+            const float *q0 = Qs + (2 * ty) * kRowP, *q1 = q0 + kRowP;
+#pragma unroll 4
+            for (int k = 0; k < kDk; k += 4) {
+                const float4 a0 = ld4(w0 + k), a1 = ld4(w1 + k), b0 = ld4(q0 + k), b1 = ld4(q1 + k);
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    const float4 sv = ld4(S + (tx + 8 * m) * kRowP + k);
+                    d[0][m] = dot4(a0, sv, d[0][m]);
+                    d[1][m] = dot4(a1, sv, d[1][m]);
+                    qs[0][m] = dot4(b0, sv, qs[0][m]);
+                    qs[1][m] = dot4(b1, sv, qs[1][m]);
+                }
+            }
+#pragma unroll
+            for (int x = 0; x < 2; ++x)
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    const int i = 2 * ty + x, r = tx + 8 * m;
+                    d[x][m] = Us[i * kRowsScan + r] - d[x][m];
+                    Dl[i * kDP + r] = d[x][m];
+                }
+        }
+        __syncthreads();  // W, Q, U released; D complete
+        if (c + 1 < nc) {
+            issue_a(c + 1);
+            cp_async_wait<1>();  // B(c)
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float lgC = LGs[n - 1];
+        // phase 2a and the scaled copy of delta
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+            const int i = 2 * ty + x;
+            const float li = LGs[i];
+            const float ei = expf(li), ec = expf(lgC - li);
+            float acc[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                acc[m] = ei * qs[x][m];
+                Dsc[i * kDP + tx + 8 * m] = d[x][m] * ec;
+            }
+            for (int j = 0; j <= i; ++j) {
+                const float a = QKs[i * kQKP + j];
+#pragma unroll
+                for (int m = 0; m < 4; ++m) acc[m] = fmaf(a, Dl[j * kDP + tx + 8 * m], acc[m]);
+            }
+            if (i < n) {
+#pragma unroll
+                for (int m = 0; m < 4; ++m)
+                    y[(int64_t)(t0 + i) * kValDim + hv * kDv + r0 + tx + 8 * m] = f32_to_bf16_bits(acc[m]);
+            }
+        }
+        __syncthreads();  // Dsc complete
+        // phase 2b: this thread's 4 value rows x 4 keys of S
+        {
+            const float eC = expf(lgC);
+            float sacc[4][4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const float4 sv = ld4(S + (4 * tx + m) * kRowP + 4 * ty);
+                sacc[m][0] = eC * sv.x;
+                sacc[m][1] = eC * sv.y;
+                sacc[m][2] = eC * sv.z;
+                sacc[m][3] = eC * sv.w;
+            }
+#pragma unroll 8
+            for (int j = 0; j < kChunk; ++j) {
+                const float4 dj = ld4(Dsc + j * kDP + 4 * tx);
+                const float4 kj = ld4(Ks + j * kDk + 4 * ty);
+                fma4(sacc[0], dj.x, kj);
+                fma4(sacc[1], dj.y, kj);
+                fma4(sacc[2], dj.z, kj);
+                fma4(sacc[3], dj.w, kj);
+            }
+            // S is read by other threads only in phase 1, which every thread has finished; each
+            // element here has exactly one owner.
+#pragma unroll
+            for (int m = 0; m < 4; ++m)
+                *reinterpret_cast<float4 *>(S + (4 * tx + m) * kRowP + 4 * ty) =
+                    make_float4(sacc[m][0], sacc[m][1], sacc[m][2], sacc[m][3]);
+        }
+        __syncthreads();  // K, QKm, lg, D released
+        if (c + 1 < nc) issue_b(c + 1);
+    }
+    __syncthreads();
+    for (int i = tid; i < kRowsScan * kDk; i += 256) st_g[i] = S[(i / kDk) * kRowP + i % kDk];
 }
 
 }  // namespace
 
 size_t gated_delta_prefill_workspace_bytes(int tokens) {
     if (tokens <= 0) return 0;
-    return (size_t)tokens * (2 * kKeyDim + kHk + 2 * kHv) * sizeof(float);
+    const int64_t nc = (tokens + kChunk - 1) / kChunk;
+    return ((size_t)tokens * (2 * kKeyDim + 2 * kHv) + (size_t)kHv * nc * ChunkWs::kPer) * sizeof(float);
 }
 
 cudaError_t launch_conv1d_decode(float *states, int64_t num_slots, const int32_t *slots, int batch,
@@ -462,23 +705,30 @@ cudaError_t launch_gated_delta_prefill(float *state, int has_state, const uint16
                                        cudaStream_t stream) {
     float *qn = static_cast<float *>(ws);
     float *kn = qn + (size_t)T * kKeyDim;
-    float *kqn = kn + (size_t)T * kKeyDim;
-    float *g = kqn + (size_t)T * kHk;
-    float *beta = g + (size_t)T * kHv;
+    float *lgd = kn + (size_t)T * kKeyDim;
+    float *beta = lgd + (size_t)T * kHv;
+    float *cw = beta + (size_t)T * kHv;
+    const int nc = (T + kChunk - 1) / kChunk;
     cudaError_t e = launch_pdl(gated_delta_prep_kernel, dim3(T, kHk), dim3(128), 0, stream, conv_out, a, b,
-                               a_log, dt_bias, T, qn, kn, kqn, g, beta);
+                               a_log, dt_bias, T, qn, kn, lgd, beta);
     if (e != cudaSuccess) return e;
+    constexpr int kChunkSmem = kChunkSmemFloats * (int)sizeof(float);
+    constexpr int kScanSmemC = ScanSmem::kFloats * (int)sizeof(float);
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gated_delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem);
+        e = cudaFuncSetAttribute(gated_delta_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kChunkSmem);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(gated_delta_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmemC);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    return launch_pdl(gated_delta_scan_kernel, dim3(kDv / kScanRowsPerCta, kHv), dim3(kScanWarps * 32),
-                      kScanSmem, stream, state, has_state, conv_out, (const float *)qn, (const float *)kn,
-                      (const float *)kqn, (const float *)g, (const float *)beta, T, y);
+    e = launch_pdl(gated_delta_chunk_kernel, dim3(nc, kHv), dim3(256), kChunkSmem, stream, (const float *)qn,
+                   (const float *)kn, (const float *)lgd, (const float *)beta, conv_out, T, cw);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(gated_delta_chunk_scan_kernel, dim3(kDv / kRowsScan, kHv), dim3(256), kScanSmemC, stream,
+                      state, has_state, (const float *)qn, (const float *)kn, (const float *)cw, T, y);
 }
 
 cudaError_t linear_read_error(DevErrorHost *e, bool clear) {

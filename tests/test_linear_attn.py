@@ -5,9 +5,10 @@ mathematics (different summation order: agreement to float rounding), conv1d pre
 repeated decode steps (bit-exact: same products in the same order), and gated-delta prefill
 against repeated decode steps (the reference's two q/k norm reductions differ in order only).
 GPU: every entry point against the oracle on the same seeded inputs. Tolerances: conv state
-bit-exact (a copy of inputs); conv output and y within 1 bf16 ulp plus 1e-6 (the only
-differences are CUDA's expf/logf against libm's, feeding SiLU, softplus and the gates);
-recurrent state within 1e-5 relative + 1e-6 absolute after up to 257 tokens."""
+bit-exact (a copy of inputs); conv output and y within 1 bf16 ulp plus 1e-6 (decode: only
+CUDA's expf/logf differ from libm's; prefill also regroups the recurrence into 64-token chunks,
+the same fp32 arithmetic in another order); recurrent state within 1e-5 relative + 1e-6
+absolute after up to 1600 tokens."""
 import numpy as np
 import pytest
 
@@ -163,7 +164,7 @@ def test_gated_delta_decode_batch_with_slots(cuda, oracle):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("has_state,T", [(0, 1), (1, 5), (0, 257)])
+@pytest.mark.parametrize("has_state,T", [(0, 1), (1, 5), (0, 257), (1, 1600)])
 def test_gated_delta_prefill(cuda, oracle, has_state, T):
     import torch
     from _util import dev
@@ -183,8 +184,11 @@ def test_gated_delta_prefill(cuda, oracle, has_state, T):
 
 
 @pytest.mark.gpu
-def test_gated_delta_prefill_in_two_chunks_is_bit_exact(cuda, oracle):
-    """The scan carries its state across calls exactly: 100 + 60 tokens == 160 tokens."""
+@pytest.mark.parametrize("cut", [128, 100])
+def test_gated_delta_prefill_across_calls(cuda, oracle, cut):
+    """The state carries across calls: prefill of 160 tokens against `cut` + the rest. At a
+    64-token chunk boundary (128) the arithmetic is the same, so the results are bitwise equal;
+    elsewhere (100) the chunks regroup the same fp32 recurrence, within the state tolerance."""
     import torch
     from _util import dev
     T = 160
@@ -196,8 +200,12 @@ def test_gated_delta_prefill_in_two_chunks_is_bit_exact(cuda, oracle):
     cuda.gated_delta_prefill(s1, 0, dev(conv_out), dev(a), dev(b), al, dev(dt_bias), y1, ws)
     s2 = torch.zeros_like(s1)
     y2 = torch.empty_like(y1)
-    for lo, hi, has in [(0, 100, 0), (100, 160, 1)]:
+    for lo, hi, has in [(0, cut, 0), (cut, T, 1)]:
         cuda.gated_delta_prefill(s2, has, dev(conv_out[lo:hi]), dev(a[lo:hi]), dev(b[lo:hi]), al,
                                  dev(dt_bias), y2[lo:hi], ws)
     torch.cuda.synchronize()
-    assert torch.equal(s1, s2) and torch.equal(y1, y2)
+    if cut % 64 == 0:
+        assert torch.equal(s1, s2) and torch.equal(y1, y2)
+    else:
+        assert np.allclose(s2.cpu().numpy(), s1.cpu().numpy(), rtol=1e-5, atol=1e-6)
+        _close_bf16(_bf(oracle, y2.cpu().numpy().view(np.uint16)), _bf(oracle, y1.cpu().numpy().view(np.uint16)), "y")
