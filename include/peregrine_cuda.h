@@ -69,7 +69,8 @@ const char *pgc_status_string(int status);
 /* Library ABI version (major*10000 + minor*100 + patch). */
 int pgc_version(void);
 /* Reads and optionally clears the device error word of the current device: 0 when no kernel
- * recorded a fault. Synchronises the device. Replaces the reference's
+ * recorded a fault, else code + 100 * unit (units: 0 decode and context-parallel exchange,
+ * 1 append, 2 copies, 3 prefill, 4 linear attention, 5 q4 projection). Synchronises the device. Replaces the reference's
  * MTLCommandBufferStatusError check at commit time (bridge.m:376). */
 int pgc_device_error(int *code_out, int64_t *detail_out, int clear);
 
@@ -545,9 +546,11 @@ int pgc_q4_dequantize(const uint32_t *weight, const uint16_t *scales, const uint
                       uint16_t *out, int out_dim, int in_dim, void *stream);
 
 /* linear_q4_affine_group64_qmv_fast_bf16 (linear.metal:158-194) for decode batches:
- * y[t][o] = sum_k x[t][k] * w[o][k], x [tokens][in] bf16, y [tokens][out] bf16, fp32 sums over
- * the bf16-rounded dequantised weights. in_dim a multiple of 2048 up to 8192, out_dim % 64 ==
- * 0; x and weight 16-byte aligned. Best for up to 64 tokens per call (HBM-bound on the packed weights). */
+ * y[t][o] = sum_k x[t][k] * w[o][k], x [tokens][in] bf16, y [tokens][out] bf16, in fp32 with the
+ * reference decode algebra per 64-input group (scale * sum(q x) + bias * sum(x), unrounded
+ * weights). in_dim a multiple of 2048 up to 8192, out_dim % 64 == 0; x, weight, scales and
+ * biases 16-byte aligned. Up to 64 tokens share one pass over the packed weights; larger
+ * batches take one pass per 64 tokens. */
 int pgc_q4_linear(const uint16_t *x, int tokens, const uint32_t *weight, const uint16_t *scales,
                   const uint16_t *biases, uint16_t *y, int out_dim, int in_dim, void *stream);
 

@@ -12,7 +12,9 @@
 
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <unordered_map>
 
 #include "pgc_internal.h"
@@ -146,6 +148,47 @@ int q_tensor_map(const void *q, int tokens, CUtensorMap *out) {
     return PGC_OK;
 }
 
+// 2-D tiled tensor map over a row-major [outer][inner] array (elem_bytes 2 or 4), cached by
+// pointer and shape. Used by the q4 projection for its activations and packed weights.
+int tiled_map_2d(const void *ptr, int elem_bytes, int64_t inner, int64_t outer, int box_inner,
+                 int box_outer, bool swizzle128, CUtensorMap *out) {
+    int dev = 0;
+    int st = check_device(&dev);
+    if (st != PGC_OK) return st;
+    struct Key {
+        int dev;
+        const void *ptr;
+        int64_t a, b, c;
+        bool operator<(const Key &o) const {
+            return std::tie(dev, ptr, a, b, c) < std::tie(o.dev, o.ptr, o.a, o.b, o.c);
+        }
+    };
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{dev, ptr, inner * 8 + elem_bytes, outer, (int64_t)box_inner << 32 | box_outer << 1 | (swizzle128 ? 1 : 0)};
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return PGC_OK;
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return PGC_ERR_CUDA;
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    const cuuint64_t strides[1] = {(cuuint64_t)(inner * elem_bytes)};
+    const cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(&m, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 2,
+                    const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return PGC_ERR_CUDA;
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return PGC_OK;
+}
+
 }  // namespace pgc
 
 using namespace pgc;
@@ -176,16 +219,17 @@ int pgc_device_error(int *code_out, int64_t *detail_out, int clear) {
     int st = check_device(nullptr);
     if (st != PGC_OK) return st;
     if (cudaDeviceSynchronize() != cudaSuccess) return PGC_ERR_CUDA;
-    DevErrorHost e[5] = {};
+    DevErrorHost e[6] = {};
     cudaError_t r = decode_read_error(&e[0], clear != 0);
     if (r == cudaSuccess) r = append_read_error(&e[1], clear != 0);
     if (r == cudaSuccess) r = copy_read_error(&e[2], clear != 0);
     if (r == cudaSuccess) r = prefill_read_error(&e[3], clear != 0);
     if (r == cudaSuccess) r = linear_read_error(&e[4], clear != 0);
+    if (r == cudaSuccess) r = q4_read_error(&e[5], clear != 0);
     if (r != cudaSuccess) return PGC_ERR_CUDA;
     int code = 0;
     long long detail = 0;
-    for (int i = 0; i < 5 && code == 0; ++i)
+    for (int i = 0; i < 6 && code == 0; ++i)
         if (e[i].code != 0) {
             code = e[i].code + 100 * i;  // unit in the hundreds digit
             detail = e[i].detail;
@@ -632,14 +676,18 @@ int pgc_q4_linear(const uint16_t *x, int tokens, const uint32_t *weight, const u
     int st = check_device(nullptr);
     if (st != PGC_OK) return st;
     if (tokens < 0 || out_dim <= 0 || in_dim <= 0) return PGC_ERR_INVALID;
-    // 8 K slices of whole 64-input groups, a multiple of 4 groups each (8-byte metadata copies)
+    // K slices of whole 8-group units (16-byte scale and bias copies); the scale and bias
+    // slices of a CTA stay in shared memory, which bounds in_dim
     if (in_dim % 2048 != 0 || in_dim > 8192 || out_dim % 64 != 0) return PGC_ERR_INVALID;
     if (tokens == 0) return PGC_OK;
     if (!x || !weight || !scales || !biases || !y) return PGC_ERR_INVALID;
-    if (!al16(x) || !al16(weight) || ((uintptr_t)scales & 7u) != 0 || ((uintptr_t)biases & 7u) != 0 ||
-        ((uintptr_t)y & 3u) != 0)
+    if (!al16(x) || !al16(weight) || !al16(scales) || !al16(biases) || ((uintptr_t)y & 1u) != 0)
         return PGC_ERR_ALIGN;
-    return cuda_status(launch_q4_linear(x, tokens, weight, scales, biases, y, out_dim, in_dim,
+    const int np = q4_token_tile(tokens);
+    CUtensorMap tx, tw;
+    if ((st = tiled_map_2d(x, 2, in_dim, tokens, 64, np, true, &tx)) != PGC_OK) return st;
+    if ((st = tiled_map_2d(weight, 4, in_dim / 8, out_dim, 32, 128, true, &tw)) != PGC_OK) return st;
+    return cuda_status(launch_q4_linear(tx, tw, tokens, scales, biases, y, out_dim, in_dim,
                                         static_cast<cudaStream_t>(stream)));
 }
 

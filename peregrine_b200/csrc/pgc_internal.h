@@ -24,6 +24,8 @@ int current_sm_count();
 // Tensor map over a chunk's queries [tokens][16][256] bf16 viewed as (dim, head, token),
 // 64 x 4 x 32 boxes, 128-byte swizzle. Cached per (device, pointer, tokens).
 int q_tensor_map(const void *q, int tokens, CUtensorMap *out);
+int tiled_map_2d(const void *ptr, int elem_bytes, int64_t inner, int64_t outer, int box_inner,
+                 int box_outer, bool swizzle128, CUtensorMap *out);
 
 // decode_attn.cu
 struct DecodePlan {
@@ -110,8 +112,11 @@ cudaError_t linear_read_error(DevErrorHost *e, bool clear);
 // q4_linear.cu
 cudaError_t launch_q4_dequantize(const uint32_t *w, const uint16_t *scales, const uint16_t *biases,
                                  uint16_t *out, int out_dim, int in_dim, cudaStream_t stream);
-cudaError_t launch_q4_linear(const uint16_t *x, int T, const uint32_t *w, const uint16_t *scales,
+// Token rows per q4 projection tile (the MMA's N): 16, 32 or 64.
+inline int q4_token_tile(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : 64; }
+cudaError_t launch_q4_linear(const CUtensorMap &tx, const CUtensorMap &tw, int T, const uint16_t *scales,
                              const uint16_t *biases, uint16_t *y, int out_dim, int in_dim,
                              cudaStream_t stream);
+cudaError_t q4_read_error(DevErrorHost *e, bool clear);
 
 }  // namespace pgc

@@ -9,15 +9,10 @@
 // (linear_q4_affine_group64_qmv_fast_bf16), prefill dequantises each weight once into a dense
 // bf16 matrix (q4_affine_group64_dequantize_bf16, linear.metal:422-444) and runs a dense GEMM.
 //
-// q4_linear_kernel is the decode projection, 64 tokens per CTA row of the grid. It is HBM-bound
-// on the packed weights (0.5 byte per weight, read once), so what matters is bytes in flight:
-// an 8-CTA cluster splits K, every CTA loads its whole slice (64 output rows x in/8 inputs) at
-// once, and the slices are summed through distributed shared memory. Each warp owns 8 output
-// rows (one n8 tile) and all token tiles, dequantises its B fragments straight from the packed
-// words with one OR per pair (bf16 128 + q) and accumulates with bf16 mma.sync in fp32; per
-// 64-input group it applies scale and bias algebraically, as the reference's decode kernel
-// does (linear.metal:64-123). At 64 tokens each weight feeds 64 FMAs, more than the CUDA cores
-// could sustain at HBM speed.
+// q4_tc_kernel is the decode projection on the tcgen05 tensor cores: the packed weights are read
+// once (0.5 byte per weight) and unpacked in shared memory into the MMA's A operand, the tokens
+// are its B operand, and the per-group scale and bias are applied to the fp32 partial sums in
+// TMEM as the reference's decode kernel applies them (linear.metal:64-123).
 #include "pgc_common.cuh"
 #include "pgc_internal.h"
 
@@ -25,40 +20,11 @@ namespace pgc {
 namespace {
 
 constexpr int kQ4Group = 64;
-// A CTA has W warps of 8 output rows each: 64 rows for small batches, 128 above 16 tokens
-// (the activation block is re-read once per row tile, so wider tiles cut its L2 traffic).
-constexpr int kQ4Tokens = 64;       // token rows per CTA (4 m16 tiles)
-constexpr int kQ4Splits = 8;        // K splits = CTAs of a cluster
 
-// Token rows per CTA: the batch rounded up to whole m16 tiles, at most 64.
-__host__ __device__ inline int q4_tokens_per_cta(int T) {
-    const int r = (T + 15) / 16 * 16;
-    return r < kQ4Tokens ? r : kQ4Tokens;
-}
-
-// Shared memory of one CTA for a K slice of ks inputs and tp token rows.
-template <int W>
-struct Q4Layout {
-    static constexpr int kRows = 8 * W;
-    int xld, wld, x, w, sc, bi, xsum, red, bytes;
-    __host__ __device__ Q4Layout(int ks, int tp) {
-        xld = ks + 8;      // padded activation row (bf16): conflict-free ldmatrix
-        wld = ks / 8 + 4;  // padded packed-word row: a warp's 8 rows fall 4 banks apart
-        x = 0;
-        w = x + tp * xld * 2;
-        sc = w + kRows * wld * 4;
-        bi = sc + kRows * (ks / kQ4Group) * 2;
-        xsum = (bi + kRows * (ks / kQ4Group) * 2 + 15) & ~15;
-        red = xsum + tp * (ks / kQ4Group) * 4;
-        bytes = red + tp * kRows * 4;
-    }
-};
-
-__device__ __forceinline__ void cpa16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cpa8(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void cp_async16_zfill_q4(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
 }
 __device__ __forceinline__ uint32_t q4_cluster_map(uint32_t saddr, uint32_t rank) {
     uint32_t r;
@@ -109,144 +75,435 @@ __device__ __forceinline__ uint32_t nib2_bf16(uint32_t word, int j) {
     return ((t & 0xFu) | ((t & 0xF0u) << 12)) | 0x43004300u;
 }
 
-// y[t][o] = sum_k x[t][k] * w[o][k], with the reference decode path's algebra per 64-input
-// group: y += scale * sum(q * x) + bias * sum(x). The mma sees the nibbles as bf16 128 + q (exact)
-// against the bf16 activations, so it accumulates sum((128 + q) x) exactly in fp32 per group;
-// then acc += scale * tmp + (bias - 128 scale) * sum(x). Grid (8 K splits, out_dim / 64,
-// ceil(T / 64)); the 8 CTAs of a cluster split K. Each CTA issues every load of its slice at
-// once (no loop-carried pipeline: the whole slice in flight), parks its fp32 tile
-// [tokens][64 rows] in shared memory, and after a cluster barrier CTA r sums output rows
-// [8r, 8r + 8) over the 8 tiles through distributed shared memory, in rank order.
-template <int W>
-__global__ void __cluster_dims__(kQ4Splits, 1, 1) __launch_bounds__(W * 32)
-    q4_linear_kernel(const uint16_t *x, int T, const uint32_t *w, const uint16_t *scales,
-                     const uint16_t *biases, uint16_t *y, int out_dim, int in_dim) {
+// ------------------------------------------------------------------ tcgen05 pieces (cta_group::1)
+__device__ __forceinline__ uint64_t q4_sdesc(uint32_t saddr) {
+    // K-major operand, SWIZZLE_128B: 128-byte rows, 8-row atoms of 1024 B (SBO), version 1
+    return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)(16 >> 4) << 16) |
+           ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+// kind::f16 instruction descriptor: f32 accumulate, bf16 A and B, both K-major
+__host__ __device__ constexpr uint32_t q4_idesc(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void q4_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void q4_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void q4_tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void q4_tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// N consecutive fp32 columns of this warp's 32 TMEM lanes (thread i: lane quarter*32 + i)
+template <int N>
+__device__ __forceinline__ void q4_tmem_ld(uint32_t taddr, float *v);
+template <>
+__device__ __forceinline__ void q4_tmem_ld<8>(uint32_t taddr, float *v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                   "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void q4_tmem_ld<16>(uint32_t taddr, float *v) {
+    uint32_t r[16];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+                 "%11, %12, %13, %14, %15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                   "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+                   "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+PGC_DEFINE_ERROR_WORD(g_q4_err);
+
+#ifdef PGC_Q4_TRACE
+// Diagnostic build only: clock64 of each role's milestones per group in CTA (0, 0, 0).
+static __device__ long long g_q4_trace[10][128];
+#define Q4_TRACE(ev, j)                                                                       \
+    do {                                                                                      \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) < 128)              \
+            g_q4_trace[ev][j] = clock64();                                                    \
+    } while (0)
+#else
+#define Q4_TRACE(ev, j) \
+    do {                \
+    } while (0)
+#endif
+
+__device__ __forceinline__ bool q4_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int where) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (global_timer_ns() - t0 > 2000000000ull || i > (1u << 30)) {
+                record_error(&g_q4_err, kErrWaitTimeout, where);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// q4 projection on the 5th-generation tensor cores. y[t][o] = sum_k x[t][k] w[o][k] with the
+// reference decode path's algebra per 64-input group g (linear.metal:64-123):
+//   y += scale_g * sum_g(q x) + bias_g * sum_g(x).
+// The weights are the MMA's A operand (M = 128 output rows per CTA) as bf16 128 + q (exact), the
+// tokens its B operand (N = NP, the batch padded to 16, 32 or 64). Per group the tensor cores
+// give tmp = sum_g((128 + q) x) in fp32 in TMEM; the epilogue adds scale * tmp + (bias -
+// 128 scale) * sum_g(x) to fp32 registers. Grid (S, out / 128, ceil(T / NP)); the S CTAs of a
+// cluster split K and their fp32 tiles are summed through distributed shared memory in rank
+// order.
+// Warps: 0-7 epilogue (warp w reads TMEM lanes 32 (w % 4).. and token half w / 4), 8 MMA issue
+// and TMEM owner, 9-16 converters (thread c: output row c % 128, words 4 (c / 128)..+3 of a
+// group), 17-18 x sums (token halves), 19 TMA producer. The pipeline moves in steps of two
+// groups (a step's waits, proxy fence and commits are paid once per 128 inputs):
+//   - W ring: the packed words of 4 groups (2 steps) per slot ([128 rows][128 B], 128-byte
+//     swizzle, so a request moves 128 contiguous bytes of a row), 3 slots ahead; the converters
+//     release a slot when they have unpacked its last step;
+//   - X ring: one step's two x tiles (the MMA's B operands, [NP][64] bf16 swizzled, rows past T
+//     read as zero) and their sums per slot; released by the MMA's commit and the epilogue;
+//   - bf16 slots: one step's two weight tiles (the MMA's A operands, [128][64] swizzled);
+//   - TMEM: two buffers of a step's two partial-sum tiles [128 lanes][NP].
+// Each converter warp unpacks its rows on its own (no barrier across the converters) and issues
+// no copies, so the proxy fence that hands its stores to the tensor cores has nothing in flight
+// to wait for.
+template <int NP>
+struct Q4TcCfg {
+    static constexpr int kGW = 4;                       // groups per W slot
+    static constexpr int kNW = 4;                       // W slots
+    static constexpr int kLAW = kNW - 1;                // W slots loaded ahead
+    static constexpr int kNX = NP == 64 ? 3 : 4;        // X slots (steps)
+    static constexpr int kLAX = kNX - 1;                // steps of x loaded ahead
+    static constexpr int kNB = 2;                       // bf16 slots (steps)
+    static constexpr int kTB = 2;                       // TMEM buffers (steps)
+    static constexpr int kXBytes = NP * 128;            // one x tile [NP][64] bf16, swizzled
+    static constexpr int kXSum = 2 * kXBytes;           // offset of the x sums [2][NP] in a slot
+    static constexpr int kXStride = (2 * kXBytes + 2 * NP * 4 + 1023) / 1024 * 1024;
+    static constexpr int kBf = 0;                       // [kNB][2][128][64] bf16
+    static constexpr int kW = kBf + kNB * 32768;        // [kNW][128][32] u32
+    static constexpr int kX = kW + kNW * 16384;         // [kNX] x slots
+    static constexpr int kSc = kX + kNX * kXStride;     // scales, then biases
+    static constexpr int kTmemCols = kTB * 2 * NP < 32 ? 32 : kTB * 2 * NP;
+    static constexpr int kMaxG = 64;  // groups per CTA slice (scales and biases in shared memory)
+    static constexpr int kThreads = 20 * 32;
+    static_assert(NP * 128 * 4 <= kNB * 32768, "split-K tile fits in the bf16 slots");
+    // scales/biases: [128][G] u16 rows padded to 16 bytes; barriers after them
+    __host__ __device__ static int sc_ld(int G) { return G * 2 + 16; }
+    __host__ __device__ static int bars(int G) { return kSc + 2 * 128 * sc_ld(G); }
+    __host__ __device__ static int bytes(int G) { return bars(G) + 1024; }
+};
+
+template <int NP>
+__global__ void __launch_bounds__(20 * 32, 1)
+    q4_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, int T,
+                 const uint16_t *scales, const uint16_t *biases, uint16_t *y, int out_dim, int in_dim,
+                 int S) {
+    using C = Q4TcCfg<NP>;
     pdl_trigger();
     pdl_wait();
-    extern __shared__ __align__(16) uint8_t q4_smem[];
-    const int ks_len = in_dim / kQ4Splits;
-    const int tp = q4_tokens_per_cta(T);
-    constexpr int kQ4RowsPerCta = 8 * W;
-    constexpr int kQ4Warps = W;
-    const Q4Layout<W> L(ks_len, tp);
-    uint16_t *xs = reinterpret_cast<uint16_t *>(q4_smem + L.x);
-    uint32_t *ws_ = reinterpret_cast<uint32_t *>(q4_smem + L.w);
-    uint16_t *scs = reinterpret_cast<uint16_t *>(q4_smem + L.sc);
-    uint16_t *bis = reinterpret_cast<uint16_t *>(q4_smem + L.bi);
-    float *xsum = reinterpret_cast<float *>(q4_smem + L.xsum);
-    float *red = reinterpret_cast<float *>(q4_smem + L.red);
+    extern __shared__ __align__(1024) uint8_t q4_smem[];
+    if ((smem_u32(q4_smem) & 1023u) != 0) {
+        if (threadIdx.x == 0) record_error(&g_q4_err, kErrSmemAlign, 0);
+        return;
+    }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int split = blockIdx.x;  // == rank in the cluster
-    const int o0 = blockIdx.y * kQ4RowsPerCta;
-    const int t0 = blockIdx.z * tp;
-    const int nt = min(tp, T - t0);
-    const int mtiles = (nt + 15) / 16;
-    const int words = in_dim / 8, groups = in_dim / kQ4Group;
-    const int k0 = split * ks_len;
-    const int wpr = ks_len / 8, gpr = ks_len / kQ4Group;  // words and groups per row in the slice
-
-    for (int i = tid; i < nt * (ks_len / 8); i += kQ4Warps * 32) {
-        const int r = i / (ks_len / 8), u = i % (ks_len / 8);
-        cpa16(xs + r * L.xld + u * 8, x + (int64_t)(t0 + r) * in_dim + k0 + u * 8);
-    }
-    for (int i = tid; i < kQ4RowsPerCta * (wpr / 4); i += kQ4Warps * 32) {
-        const int r = i / (wpr / 4), u = i % (wpr / 4);
-        cpa16(ws_ + r * L.wld + u * 4, w + (int64_t)(o0 + r) * words + k0 / 8 + u * 4);
-    }
-    for (int i = tid; i < kQ4RowsPerCta * (gpr / 4); i += kQ4Warps * 32) {
-        const int r = i / (gpr / 4), u = i % (gpr / 4);
-        const int64_t gi = (int64_t)(o0 + r) * groups + k0 / kQ4Group + u * 4;
-        cpa8(scs + r * gpr + u * 4, scales + gi);
-        cpa8(bis + r * gpr + u * 4, biases + gi);
-    }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    // sum(x) of every (token, group) of the slice: a warp per pair, each lane one bf16 pair
-    for (int i = warp; i < tp * gpr; i += kQ4Warps) {
-        const int r = i / gpr, g = i % gpr;
-        float sx = 0.f;
-        if (r < nt) {
-            const uint32_t v = *reinterpret_cast<const uint32_t *>(xs + r * L.xld + g * kQ4Group + 2 * lane);
-            sx = bf16_bits_to_f32(v & 0xFFFFu) + bf16_bits_to_f32(v >> 16);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    if (tid == 0) Q4_TRACE(8, 0);
+    const int split = blockIdx.x;  // rank in the cluster
+    const int o0 = blockIdx.y * 128;
+    const int t0 = blockIdx.z * NP;
+    const int nt = min(NP, T - t0);
+    const int groups = in_dim / kQ4Group;
+    const int G = groups / S;  // groups of this CTA's K slice (a multiple of 8)
+    const int nsteps = G / 2;
+    const int g0 = split * G;
+    const int ldsc = C::sc_ld(G);
+    uint16_t *scs = reinterpret_cast<uint16_t *>(q4_smem + C::kSc);
+    uint16_t *bis = reinterpret_cast<uint16_t *>(q4_smem + C::kSc + 128 * ldsc);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(q4_smem + C::bars(G));
+    uint64_t *conv_full = bar, *bf_empty = conv_full + C::kNB;
+    uint64_t *tmem_full = bf_empty + C::kNB, *tmem_empty = tmem_full + C::kTB;
+    uint64_t *w_full = tmem_empty + C::kTB, *w_empty = w_full + C::kNW;
+    uint64_t *x_full = w_empty + C::kNW, *x_empty = x_full + C::kNX, *xs_full = x_empty + C::kNX;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xs_full + C::kNX);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(xs_full + C::kNX + 1);
+    if (tid == 0) {
+        for (int i = 0; i < C::kNB; ++i) {
+            mbar_init(&conv_full[i], 8);
+            mbar_init(&bf_empty[i], 1);
         }
-        if (lane == 0) xsum[i] = sx;
+        for (int i = 0; i < C::kTB; ++i) {
+            mbar_init(&tmem_full[i], 1);
+            mbar_init(&tmem_empty[i], 8);
+        }
+        for (int i = 0; i < C::kNW; ++i) {
+            mbar_init(&w_full[i], 1);
+            mbar_init(&w_empty[i], 8);
+        }
+        for (int i = 0; i < C::kNX; ++i) {
+            mbar_init(&x_full[i], 1);
+            mbar_init(&x_empty[i], 9);
+            mbar_init(&xs_full[i], 2);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
     }
+    if (warp == 8) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"(C::kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    q4_tc_fence_before();
     __syncthreads();
+    q4_tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (tid == 0) Q4_TRACE(8, 1);
+    const uint32_t sbase = smem_u32(q4_smem);
+    auto x_slot = [&](int st) { return C::kX + (st % C::kNX) * C::kXStride; };
 
-    float acc[4][4];
+    constexpr int kHalf = NP / 2;                 // tokens per epilogue warp
+    constexpr int kCh = kHalf < 16 ? kHalf : 16;  // TMEM columns per load
+    float acc[kHalf];
 #pragma unroll
-    for (int m = 0; m < 4; ++m)
+    for (int i = 0; i < kHalf; ++i) acc[i] = 0.f;
+    const int q = warp & 3, h = (warp >> 2) & 1;
+    const int erow = 32 * q + lane;  // epilogue: output row within the tile
+
+    if (warp < 8) {
+        // ------------------------------------------------ epilogue
+        {
+            // this slice's scales (token half 0) or biases (half 1) of row erow
+            const bool ok = o0 + erow < out_dim;
+            const uint16_t *src = (h == 0 ? scales : biases) + (int64_t)(o0 + erow) * groups + g0;
+            uint8_t *dst = q4_smem + C::kSc + h * 128 * ldsc + erow * ldsc;
+            for (int u = 0; u < G / 8; ++u)
+                cp_async16_zfill_q4(dst + 16 * u, ok ? src + 8 * u : scales, ok);
+            asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+            asm volatile("bar.sync 2, 256;" ::: "memory");
+            if (tid == 0) Q4_TRACE(8, 2);
+        }
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16) + h * kHalf;
+        for (int st = 0; st < nsteps; ++st) {
+            const int b = st % C::kTB;
+            if (!q4_wait(&tmem_full[b], (st / C::kTB) & 1, abort_flag, 30)) break;
+            if (!q4_wait(&xs_full[st % C::kNX], (st / C::kNX) & 1, abort_flag, 31)) break;
+            if (tid == 0) Q4_TRACE(6, st);
+            q4_tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[m][i] = 0.f;
-    const int n_local = warp * 8 + (lane >> 2);  // this thread's B column (output row)
-    const int tq = lane & 3;
-    const int c0 = warp * 8 + 2 * tq;            // this thread's two C columns (output rows)
-    const uint32_t *wrow = ws_ + n_local * L.wld;
-    for (int g = 0; g < gpr; ++g) {
-        float tmp[4][4];
+            for (int jg = 0; jg < 2; ++jg) {
+                const int g = 2 * st + jg;
+                const float sc = bf16_bits_to_f32(scs[erow * (ldsc / 2) + g]);
+                const float e = bf16_bits_to_f32(bis[erow * (ldsc / 2) + g]) - 128.0f * sc;
+                const float *xs = reinterpret_cast<const float *>(q4_smem + x_slot(st) + C::kXSum) + jg * NP + h * kHalf;
 #pragma unroll
-        for (int m = 0; m < 4; ++m)
+                for (int c0 = 0; c0 < kHalf; c0 += kCh) {
+                    float tmp[kCh];
+                    q4_tmem_ld<kCh>(lane_addr + (b * 2 + jg) * NP + c0, tmp);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) tmp[m][i] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < kQ4Group / 16; ++kk) {
-            const int ks = g * (kQ4Group / 16) + kk;
-            const uint2 wq = *reinterpret_cast<const uint2 *>(wrow + 2 * ks);  // one 8-byte load
-            const uint32_t b0 = nib2_bf16(wq.x, tq), b1 = nib2_bf16(wq.y, tq);
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                if (m < mtiles) {
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4(smem_u32(xs + (m * 16 + (lane & 15)) * L.xld + ks * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
-                    mma_bf16_16816(tmp[m], a0, a1, a2, a3, b0, b1);
+                    for (int i = 0; i < kCh; i += 4) {
+                        const float4 v = *reinterpret_cast<const float4 *>(xs + c0 + i);
+                        acc[c0 + i] = fmaf(sc, tmp[i], fmaf(e, v.x, acc[c0 + i]));
+                        acc[c0 + i + 1] = fmaf(sc, tmp[i + 1], fmaf(e, v.y, acc[c0 + i + 1]));
+                        acc[c0 + i + 2] = fmaf(sc, tmp[i + 2], fmaf(e, v.z, acc[c0 + i + 2]));
+                        acc[c0 + i + 3] = fmaf(sc, tmp[i + 3], fmaf(e, v.w, acc[c0 + i + 3]));
+                    }
                 }
             }
+            q4_tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&tmem_empty[b]);
+                mbar_arrive(&x_empty[st % C::kNX]);
+            }
+            if (tid == 0) Q4_TRACE(7, st);
         }
-        const float s0 = bf16_bits_to_f32(scs[c0 * gpr + g]), s1 = bf16_bits_to_f32(scs[(c0 + 1) * gpr + g]);
-        const float e0 = bf16_bits_to_f32(bis[c0 * gpr + g]) - 128.0f * s0;
-        const float e1 = bf16_bits_to_f32(bis[(c0 + 1) * gpr + g]) - 128.0f * s1;
+        if (S == 1 && o0 + erow < out_dim) {
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            if (m < mtiles) {
-                const int r0 = m * 16 + (lane >> 2);
-                const float x0 = xsum[r0 * gpr + g], x1 = xsum[(r0 + 8) * gpr + g];
-                acc[m][0] += s0 * tmp[m][0] + e0 * x0;
-                acc[m][1] += s1 * tmp[m][1] + e1 * x0;
-                acc[m][2] += s0 * tmp[m][2] + e0 * x1;
-                acc[m][3] += s1 * tmp[m][3] + e1 * x1;
+            for (int i = 0; i < kHalf; ++i) {
+                const int t = h * kHalf + i;
+                if (t < nt) y[(int64_t)(t0 + t) * out_dim + o0 + erow] = f32_to_bf16_bits(acc[i]);
             }
         }
-    }
-    // C fragment: tokens lane/4 and lane/4 + 8 of the m tile, rows 2*(lane%4) + {0, 1} of the n8
+    } else if (warp == 8) {
+        // ------------------------------------------------ MMA issue (one thread)
+        int last = -1;
+        if (lane == 0) {
+            constexpr uint32_t idesc = q4_idesc(128, NP);
+            for (int st = 0; st < nsteps; ++st) {
+                const int bs = st % C::kNB, b = st % C::kTB, xs = st % C::kNX;
+                if (!q4_wait(&conv_full[bs], (st / C::kNB) & 1, abort_flag, 20)) break;
+                Q4_TRACE(3, st);
+                if (!q4_wait(&x_full[xs], (st / C::kNX) & 1, abort_flag, 22)) break;
+                if (!q4_wait(&tmem_empty[b], ((st / C::kTB) & 1) ^ 1, abort_flag, 21)) break;
+                Q4_TRACE(4, st);
+                q4_tc_fence_after();
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        if (m < mtiles) {
-            const int r0 = m * 16 + (lane >> 2);
-            red[r0 * kQ4RowsPerCta + c0] = acc[m][0];
-            red[r0 * kQ4RowsPerCta + c0 + 1] = acc[m][1];
-            red[(r0 + 8) * kQ4RowsPerCta + c0] = acc[m][2];
-            red[(r0 + 8) * kQ4RowsPerCta + c0 + 1] = acc[m][3];
+                for (int jg = 0; jg < 2; ++jg) {
+                    const uint32_t a_addr = sbase + C::kBf + bs * 32768 + jg * 16384;
+                    const uint32_t x_addr = sbase + x_slot(st) + jg * C::kXBytes;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        q4_mma(tmem + (b * 2 + jg) * NP, q4_sdesc(a_addr + kk * 32), q4_sdesc(x_addr + kk * 32),
+                               idesc, kk > 0 ? 1u : 0u);
+                }
+                q4_commit(&bf_empty[bs]);
+                q4_commit(&x_empty[xs]);
+                q4_commit(&tmem_full[b]);
+                Q4_TRACE(5, st);
+                last = st;
+            }
+            // the tensor cores are done with everything issued before TMEM is released
+            if (last >= 0 && *abort_flag) mbar_wait_bounded(&tmem_full[last % C::kTB], (last / C::kTB) & 1);
+        }
+        __syncwarp();
+    } else if (warp < 17) {
+        // ------------------------------------------------ converters (each warp on its own)
+        const int c = tid - 9 * 32;
+        const int row = c & 127, hh = c >> 7;
+        for (int st = 0; st < nsteps; ++st) {
+            const int bs = st % C::kNB, ws = st / 2;
+            bool ok = q4_wait(&w_full[ws % C::kNW], (ws / C::kNW) & 1, abort_flag, 12);
+            if (c == 0) Q4_TRACE(0, st);
+            if (lane == 0 && ok) ok = q4_wait(&bf_empty[bs], ((st / C::kNB) & 1) ^ 1, abort_flag, 10);
+            if (__any_sync(0xffffffffu, !ok)) break;
+            if (c == 0) Q4_TRACE(1, st);
+            // group j of the W slot: words 4 hh..4 hh+3 are 16-byte chunk 2 j + hh of the row
+            const uint8_t *wrow = q4_smem + C::kW + (ws % C::kNW) * 16384 + row * 128;
+            uint4 wq[2];
+#pragma unroll
+            for (int jg = 0; jg < 2; ++jg) {
+                const int j = 2 * (st & 1) + jg;
+                wq[jg] = *reinterpret_cast<const uint4 *>(wrow + (((2 * j + hh) ^ (row & 7)) << 4));
+            }
+#pragma unroll
+            for (int jg = 0; jg < 2; ++jg) {
+                uint8_t *bf = q4_smem + C::kBf + bs * 32768 + jg * 16384 + row * 128;
+                const uint32_t wv[4] = {wq[jg].x, wq[jg].y, wq[jg].z, wq[jg].w};
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    const int u = 4 * hh + jj;
+                    *reinterpret_cast<uint4 *>(bf + ((u ^ (row & 7)) << 4)) =
+                        make_uint4(nib2_bf16(wv[jj], 0), nib2_bf16(wv[jj], 1), nib2_bf16(wv[jj], 2), nib2_bf16(wv[jj], 3));
+                }
+            }
+            fence_proxy_async_smem();  // the bf16 tiles are read by the tensor cores
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&conv_full[bs]);
+                if (st & 1) mbar_arrive(&w_empty[ws % C::kNW]);
+            }
+            if (c == 0) Q4_TRACE(2, st);
+        }
+    } else if (warp < 19) {
+        // ------------------------------------------------ x sums: warp 17 + hx, tokens of half hx
+        const int hx = warp - 17;
+        constexpr int kLpt = 64 / NP;      // lanes per token
+        constexpr int kChunks = 8 / kLpt;  // 16-byte chunks per lane
+        const int t = hx * kHalf + lane / kLpt, part = lane % kLpt;
+        for (int st = 0; st < nsteps; ++st) {
+            const bool ok = q4_wait(&x_full[st % C::kNX], (st / C::kNX) & 1, abort_flag, 13);
+            if (__any_sync(0xffffffffu, !ok)) break;
+            uint8_t *xsl = q4_smem + x_slot(st);
+            float sx[2] = {0.f, 0.f};
+#pragma unroll
+            for (int jg = 0; jg < 2; ++jg)
+#pragma unroll
+                for (int i = 0; i < kChunks; ++i) {
+                    const int u = part * kChunks + i;
+                    const uint4 v = *reinterpret_cast<const uint4 *>(xsl + jg * C::kXBytes + t * 128 + ((u ^ (t & 7)) << 4));
+                    sx[jg] += (bf16_bits_to_f32(v.x & 0xFFFFu) + bf16_bits_to_f32(v.x >> 16)) +
+                              (bf16_bits_to_f32(v.y & 0xFFFFu) + bf16_bits_to_f32(v.y >> 16)) +
+                              (bf16_bits_to_f32(v.z & 0xFFFFu) + bf16_bits_to_f32(v.z >> 16)) +
+                              (bf16_bits_to_f32(v.w & 0xFFFFu) + bf16_bits_to_f32(v.w >> 16));
+                }
+#pragma unroll
+            for (int jg = 0; jg < 2; ++jg) {
+#pragma unroll
+                for (int o = kLpt / 2; o > 0; o >>= 1) sx[jg] += __shfl_xor_sync(0xffffffffu, sx[jg], o);
+                if (part == 0) reinterpret_cast<float *>(xsl + C::kXSum)[jg * NP + t] = sx[jg];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xs_full[st % C::kNX]);
+        }
+    } else if (lane == 0) {
+        // ------------------------------------------------ TMA producer (one thread)
+        tma_prefetch_desc(&tmx);
+        tma_prefetch_desc(&tmw);
+        const uint64_t pol_w = l2_policy_evict_first(), pol_x = l2_policy_evict_last();
+        const int nws = G / C::kGW;  // W slots of the slice
+        auto issue_w = [&](int ws) {
+            if (ws >= nws) return true;
+            const int prev = ws - C::kNW;  // the W slot's previous contents
+            if (prev >= 0 && !q4_wait(&w_empty[prev % C::kNW], (prev / C::kNW) & 1, abort_flag, 14)) return false;
+            uint64_t *fb = &w_full[ws % C::kNW];
+            mbar_arrive_expect_tx(fb, 16384);
+            tma_load_2d(q4_smem + C::kW + (ws % C::kNW) * 16384, &tmw, (g0 + ws * C::kGW) * 8, o0, fb, pol_w);
+            return true;
+        };
+        auto issue_x = [&](int st) {
+            if (st >= nsteps) return true;
+            const int prev = st - C::kNX;
+            if (prev >= 0 && !q4_wait(&x_empty[prev % C::kNX], (prev / C::kNX) & 1, abort_flag, 11)) return false;
+            uint64_t *fb = &x_full[st % C::kNX];
+            mbar_arrive_expect_tx(fb, 2 * C::kXBytes);
+            tma_load_2d(q4_smem + x_slot(st), &tmx, (g0 + 2 * st) * kQ4Group, t0, fb, pol_x);
+            tma_load_2d(q4_smem + x_slot(st) + C::kXBytes, &tmx, (g0 + 2 * st + 1) * kQ4Group, t0, fb, pol_x);
+            return true;
+        };
+        // W slots are consumed one per two steps, x slots one per step: issue in consumption
+        // order, each as soon as its slot is free
+        int nw = 0, nx = 0;
+        bool ok = true;
+        while (ok && (nw < nws || nx < nsteps)) {
+            if (nw < nws && (nx >= nsteps || 2 * nw <= nx + 2 * C::kLAW - C::kLAX)) ok = issue_w(nw++);
+            else ok = issue_x(nx++);
         }
     }
-    q4_cluster_sync();  // every CTA's tile is in its shared memory
-    {
-        // CTA `split` reduces its eighth of the output rows for all nt tokens
-        constexpr int kSlice = kQ4RowsPerCta / kQ4Splits;
-        constexpr int kTokPass = kQ4Warps * 32 / kSlice;
-        const int rr = tid % kSlice, tk = tid / kSlice;
-        const int col = split * kSlice + rr;
+
+    if (S > 1) {
+        // split-K: every CTA parks its fp32 tile [NP][128] in the (now idle) bf16 slots, then
+        // CTA `split` sums rows [split * 128 / S, ...) over the cluster in rank order
+        float *red = reinterpret_cast<float *>(q4_smem + C::kBf);
+        if (warp < 8) {
+#pragma unroll
+            for (int i = 0; i < kHalf; ++i) red[(h * kHalf + i) * 128 + erow] = acc[i];
+        }
+        q4_cluster_sync();
+        const int rows = 128 / S;
         const uint32_t base = smem_u32(red);
-        for (int t = tk; t < nt; t += kTokPass) {
+        for (int i = tid; i < rows * nt; i += C::kThreads) {
+            const int t = i / rows, r = split * rows + i % rows;
+            if (o0 + r >= out_dim) continue;
             float sum = 0.f;
-#pragma unroll
-            for (int q = 0; q < kQ4Splits; ++q)
-                sum += ld_dsmem(q4_cluster_map(base + (uint32_t)(t * kQ4RowsPerCta + col) * 4, q));
-            y[(int64_t)(t0 + t) * out_dim + o0 + col] = f32_to_bf16_bits(sum);
+            for (int qq = 0; qq < S; ++qq) sum += ld_dsmem(q4_cluster_map(base + (uint32_t)(t * 128 + r) * 4, qq));
+            y[(int64_t)(t0 + t) * out_dim + o0 + r] = f32_to_bf16_bits(sum);
         }
+        q4_cluster_sync();  // no CTA leaves while a peer may still read its tile
     }
-    q4_cluster_sync();  // no CTA leaves while a peer may still read its tile
+    if (tid == 0) Q4_TRACE(8, 3);
+    q4_tc_fence_before();
+    __syncthreads();
+    if (warp == 8) {
+        q4_tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols)
+                     : "memory");
+    }
 }
 
 }  // namespace
@@ -263,30 +520,75 @@ cudaError_t launch_q4_dequantize(const uint32_t *w, const uint16_t *scales, cons
                       words, in_dim);
 }
 
-template <int W>
-cudaError_t launch_q4_linear_w(const uint16_t *x, int T, const uint32_t *w, const uint16_t *scales,
-                               const uint16_t *biases, uint16_t *y, int out_dim, int in_dim,
-                               cudaStream_t stream) {
-    const int tp = q4_tokens_per_cta(T);
-    const Q4Layout<W> L(in_dim / kQ4Splits, tp);
-    static int attr_bytes[64] = {};  // largest dynamic shared memory set per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || attr_bytes[dev] < L.bytes) {
-        cudaError_t e = cudaFuncSetAttribute(q4_linear_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.bytes);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) attr_bytes[dev] = L.bytes;
-    }
-    return launch_pdl(q4_linear_kernel<W>, dim3(kQ4Splits, out_dim / (8 * W), (T + tp - 1) / tp), dim3(W * 32),
-                      (size_t)L.bytes, stream, x, T, w, scales, biases, y, out_dim, in_dim);
+// K splits: the smallest S in {1, 2, 4, 8} that gives ~0.8 of a wave of CTAs, keeping each
+// CTA's slice a whole number of 8-group units (16-byte scale and bias copies).
+static int q4_splits(int tiles, int groups, int sms, int max_g) {
+    int S = 1;
+    while (groups / S > max_g) S *= 2;
+    while (S < 8 && tiles * S < sms * 4 / 5 && (groups / (2 * S)) % 8 == 0 && groups % (2 * S) == 0) S *= 2;
+    return S;
 }
 
-cudaError_t launch_q4_linear(const uint16_t *x, int T, const uint32_t *w, const uint16_t *scales,
+template <int NP>
+static cudaError_t launch_q4_tc(const CUtensorMap &tx, const CUtensorMap &tw, int T, const uint16_t *scales,
+                                const uint16_t *biases, uint16_t *y, int out_dim, int in_dim,
+                                cudaStream_t stream) {
+    using C = Q4TcCfg<NP>;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int groups = in_dim / kQ4Group;
+    const int row_tiles = (out_dim + 127) / 128, tok_tiles = (T + NP - 1) / NP;
+    const int S = q4_splits(row_tiles * tok_tiles, groups, sms, C::kMaxG);
+    const int bytes = C::bytes(groups / S);
+    static int attr_bytes[64] = {};
+    if (dev < 0 || dev >= 64 || attr_bytes[dev] < bytes) {
+        cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_bytes[dev] = bytes;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S, row_tiles, tok_tiles);
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+#ifndef PGC_NO_PDL
+    cfg.numAttrs = 2;
+#else
+    cfg.numAttrs = 1;
+#endif
+    return cudaLaunchKernelEx(&cfg, q4_tc_kernel<NP>, tx, tw, T, scales, biases, y, out_dim, in_dim, S);
+}
+
+cudaError_t launch_q4_linear(const CUtensorMap &tx, const CUtensorMap &tw, int T, const uint16_t *scales,
                              const uint16_t *biases, uint16_t *y, int out_dim, int in_dim,
                              cudaStream_t stream) {
-    if (T > 16 && out_dim % 128 == 0)
-        return launch_q4_linear_w<16>(x, T, w, scales, biases, y, out_dim, in_dim, stream);
-    return launch_q4_linear_w<8>(x, T, w, scales, biases, y, out_dim, in_dim, stream);
+    switch (q4_token_tile(T)) {
+        case 16: return launch_q4_tc<16>(tx, tw, T, scales, biases, y, out_dim, in_dim, stream);
+        case 32: return launch_q4_tc<32>(tx, tw, T, scales, biases, y, out_dim, in_dim, stream);
+        default: return launch_q4_tc<64>(tx, tw, T, scales, biases, y, out_dim, in_dim, stream);
+    }
+}
+
+#ifdef PGC_Q4_TRACE
+extern "C" int pgc_debug_q4_trace(long long *out) {
+    return cudaMemcpyFromSymbol(out, g_q4_trace, sizeof(g_q4_trace)) == cudaSuccess ? 0 : -4;
+}
+#endif
+
+cudaError_t q4_read_error(DevErrorHost *e, bool clear) {
+    cudaError_t r = cudaMemcpyFromSymbol(e, g_q4_err, sizeof(DevError));
+    if (r != cudaSuccess || !clear) return r;
+    DevErrorHost z = {0, 0, 0};
+    return cudaMemcpyToSymbol(g_q4_err, &z, sizeof(DevError));
 }
 
 }  // namespace pgc

@@ -4,8 +4,9 @@ CPU: the oracle's dequantisation against a numpy statement of the format (nibble
 scale and bias), and its projection against float64 sums over the unrounded weights.
 GPU: pgc_q4_dequantize bit-exact against the oracle; pgc_q4_linear against the oracle (the
 reference decode path's algebra: per group scale * sum(q x) + bias * sum(x), fp32) for the
-model's projection shapes (q|gate 4096 -> 8192, k/v 4096 -> 1024, o 4096 -> 4096) and token
-counts 1..64 plus a multi-block count. Tolerance for the projection: the GPU sums in the tensor
+model's projection shapes (q|gate 4096 -> 8192, k/v 4096 -> 1024, o 4096 -> 4096), token
+counts across the 16/32/64-token tiles plus a multi-tile count, a partial 128-row tile
+(out 192, 64) and in_dim 2048 and 8192 (every split-K cluster size). Tolerance for the projection: the GPU sums in the tensor
 cores' order, so |y - y_ref| <= 1 bf16 ulp of |y_ref| + 1e-3 * rms(y_ref)."""
 import numpy as np
 import pytest
@@ -58,10 +59,12 @@ def test_q4_dequantize_bit_exact(cuda, oracle):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("out_dim,T", [(8192, 1), (1024, 7), (1024, 64), (4096, 33), (1024, 130)])
-def test_q4_linear_matches_oracle(cuda, oracle, out_dim, T):
+@pytest.mark.parametrize("out_dim,T,in_dim", [
+    (8192, 1, 4096), (1024, 7, 4096), (1024, 16, 4096), (1024, 17, 4096), (1024, 32, 4096),
+    (4096, 33, 4096), (1024, 48, 4096), (1024, 64, 4096), (1024, 130, 4096),
+    (192, 5, 2048), (64, 64, 2048), (1024, 9, 8192), (4096, 64, 8192), (1024, 1000, 2048)])
+def test_q4_linear_matches_oracle(cuda, oracle, out_dim, T, in_dim):
     import torch
-    in_dim = 4096
     w, sc, bi = _weights(oracle, out_dim, in_dim, 10 + T)
     x = oracle.normal_bf16(T * in_dim, 20 + T).reshape(T, in_dim)
     y = torch.empty((T, out_dim), dtype=torch.int16, device="cuda")
