@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1-3 side figures")
     ap.add_argument("--only-configs", action="store_true",
                     help="time only the config 1-3 side figures (profiling aid)")
+    ap.add_argument("--profile-kernels", choices=["q4", "linear"], default=None,
+                    help="small case of the q4 decode projection or the gated-delta prefill, 3 "
+                         "launches each, for ncu captures")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="profiling aid: config 2's causal prefill on one layer, 3 launches")
     return ap.parse_args()
@@ -871,6 +874,43 @@ def profile_prefill():
     print(json.dumps({"profile": "prefill", "prefix": P, "chunk": T, "launches": 3}), flush=True)
 
 
+def profile_kernels(which):
+    """Small cases for ncu captures of the next-row kernels, 3 launches each.
+    q4: the 4096 -> 8192 q|gate projection of 64 decode tokens (q4_tc_kernel; 18 MB of packed
+    weights, scales and biases; four weight copies so that launches read from HBM).
+    linear: one gated-delta prefill layer over a 1600-token chunk (gated_delta_prep_kernel,
+    gated_delta_chunk_kernel, gated_delta_chunk_scan_kernel)."""
+    import torch
+    from peregrine_b200 import capi
+    bf = torch.bfloat16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    if which == "q4":
+        o, i, T = 8192, 4096, 64
+        ws = [torch.randint(-2 ** 31, 2 ** 31 - 1, (o, i // 8), dtype=torch.int32, device="cuda", generator=g)
+              for _ in range(4)]
+        sc = (torch.rand((o, i // 64), device="cuda", generator=g) * 0.02).to(bf)
+        bi = (torch.randn((o, i // 64), device="cuda", generator=g) * 0.05).to(bf)
+        x = torch.randn((T, i), dtype=bf, device="cuda", generator=g)
+        y = torch.empty((T, o), dtype=bf, device="cuda")
+        for k in range(3):
+            capi.q4_linear(x, ws[k], sc, bi, y)
+    else:
+        T, C, HV = 1600, capi.LIN_CONV_DIM, capi.LIN_VALUE_HEADS
+        xs = torch.randn((T, C), dtype=bf, device="cuda", generator=g)
+        at = torch.randn((T, HV), dtype=bf, device="cuda", generator=g)
+        bt = torch.randn((T, HV), dtype=bf, device="cuda", generator=g)
+        a_log = torch.randn(HV, device="cuda", generator=g) * 0.5 - 1.0
+        dtb = torch.randn(HV, dtype=bf, device="cuda", generator=g)
+        rec = torch.randn((HV, 128, 128), device="cuda", generator=g) * 0.05
+        yt = torch.empty((T, HV * 128), dtype=bf, device="cuda")
+        ws = torch.empty(capi.gated_delta_prefill_workspace_bytes(T), dtype=torch.uint8, device="cuda")
+        for _ in range(3):
+            capi.gated_delta_prefill(rec, True, xs, at, bt, a_log, dtb, yt, ws)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": which, "launches": 3}), flush=True)
+
+
 def main():
     args = parse()
     assert args.warmup >= 3 or args.impl == "reference", "at least 3 warm-up steps"
@@ -885,6 +925,9 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    if args.profile_kernels:
+        profile_kernels(args.profile_kernels)
+        return
     if args.profile_prefill:
         profile_prefill()
         return
