@@ -549,26 +549,31 @@ def bench_q4(capi, iters=20):
           for _ in range(LAYERS)]
     bi = [[(torch.randn((o, i // 64), device="cuda", generator=g) * 0.05).to(torch.bfloat16) for o, i in shapes]
           for _ in range(LAYERS)]
-    T = 64
-    x = torch.randn((T, 4096), dtype=torch.bfloat16, device="cuda", generator=g)
-    ys = [torch.empty((T, o), dtype=torch.bfloat16, device="cuda") for o, _ in shapes]
     s = torch.cuda.current_stream()
 
-    def decode_step():
-        st = torch.cuda.current_stream()
-        for l in range(LAYERS):
-            for j in range(4):
-                capi.q4_linear(x, w[l][j], sc[l][j], bi[l][j], ys[j], stream=st)
+    def decode_ms(T):
+        x = torch.randn((T, 4096), dtype=torch.bfloat16, device="cuda", generator=g)
+        ys = [torch.empty((T, o), dtype=torch.bfloat16, device="cuda") for o, _ in shapes]
 
-    # 32 small launches per step: replayed as one CUDA graph, so the figure is device time and
-    # not the Python launch rate
-    decode_step()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+        def decode_step():
+            st = torch.cuda.current_stream()
+            for l in range(LAYERS):
+                for j in range(4):
+                    capi.q4_linear(x, w[l][j], sc[l][j], bi[l][j], ys[j], stream=st)
+
+        # 32 small launches per step: replayed as one CUDA graph, so the figure is device time
+        # and not the Python launch rate
         decode_step()
-    dec_ms = _ev_time(graph.replay, iters)
-    dec_bytes = LAYERS * sum(o * i // 2 + 2 * (o * i // 64) * 2 + T * (i + o) * 2 for o, i in shapes)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            decode_step()
+        ms = _ev_time(graph.replay, iters)
+        by = LAYERS * sum(o * i // 2 + 2 * (o * i // 64) * 2 + T * (i + o) * 2 for o, i in shapes)
+        return ms, by
+
+    dec_ms, dec_bytes = decode_ms(64)
+    one_ms, one_bytes = decode_ms(1)
     dense = [torch.empty((o, i), dtype=torch.bfloat16, device="cuda") for o, i in shapes]
     for j in range(4):
         capi.q4_dequantize(w[0][j], sc[0][j], bi[0][j], dense[j], stream=s)
@@ -582,10 +587,13 @@ def bench_q4(capi, iters=20):
 
     pf_ms = _ev_time(prefill_step, max(2, iters // 4))
     flops = LAYERS * sum(2 * Tp * o * i for o, i in shapes)
-    return {"workload": "q4 projections of 8 full-attention layers: decode of 64 tokens (pgc_q4_linear), "
-                        "prefill of a 1600-token chunk (dequantised weights + cuBLAS bf16 GEMM)",
+    return {"workload": "q4 projections of 8 full-attention layers: decode of 64 tokens and of 1 token "
+                        "(pgc_q4_linear), prefill of a 1600-token chunk (dequantised weights + cuBLAS "
+                        "bf16 GEMM)",
             "decode_ms_per_step": round(dec_ms, 4), "decode_bytes": dec_bytes,
             "decode_GB_s": round(dec_bytes / (dec_ms * 1e-3) / 1e9, 1),
+            "decode_1tok_ms_per_step": round(one_ms, 4),
+            "decode_1tok_GB_s": round(one_bytes / (one_ms * 1e-3) / 1e9, 1),
             "prefill_ms_per_chunk": round(pf_ms, 3),
             "prefill_TFLOP_s": round(flops / (pf_ms * 1e-3) / 1e12, 1)}
 

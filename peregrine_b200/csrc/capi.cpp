@@ -683,6 +683,9 @@ int pgc_q4_linear(const uint16_t *x, int tokens, const uint32_t *weight, const u
     if (!x || !weight || !scales || !biases || !y) return PGC_ERR_INVALID;
     if (!al16(x) || !al16(weight) || !al16(scales) || !al16(biases) || ((uintptr_t)y & 1u) != 0)
         return PGC_ERR_ALIGN;
+    if (tokens <= kQ4GemvMaxTokens)
+        return cuda_status(launch_q4_gemv(x, tokens, weight, scales, biases, y, out_dim, in_dim,
+                                          static_cast<cudaStream_t>(stream)));
     const int np = q4_token_tile(tokens);
     CUtensorMap tx, tw;
     if ((st = tiled_map_2d(x, 2, in_dim, tokens, 64, np, true, &tx)) != PGC_OK) return st;

@@ -75,6 +75,135 @@ __device__ __forceinline__ uint32_t nib2_bf16(uint32_t word, int j) {
     return ((t & 0xFu) | ((t & 0xF0u) << 12)) | 0x43004300u;
 }
 
+// Decode projection for 1-2 tokens (the reference's single-sequence GEMV,
+// linear_q4_affine_group64_qmv_fast_bf16, linear.metal:64-123) on the CUDA cores: at this batch
+// a weight feeds T FMAs, so the kernel is a stream of packed words. Each warp owns 4 output
+// rows; lane l takes words 4l..4l+3 of every 128-word run of a row (16 bytes, half a group),
+// so a warp reads 512 contiguous bytes per row and run, and issues the loads of 4 runs (16 per
+// lane at one token) before any arithmetic. x and the CTA's scales and biases are copied to
+// shared memory once per CTA; x serves the 4 rows of every warp. Per half
+// group the lane accumulates sum((128 + q) x) (each nibble as the float 128 + q, exact) and
+// sum(x), then adds scale * that + (bias - 128 scale) * sum(x); the lanes' sums meet in a
+// butterfly at the end. Each nibble becomes the float 128 + q with one byte permute, and the
+// products run as paired fp32 FMAs, so a weight costs about two issue slots at one token.
+constexpr int kGemvRows = 4;  // output rows per warp
+// Byte k of `nibbles` (a nibble in its low 4 bits) as the float 128 + q: the byte lands in bits
+// 16-23 under the exponent byte 0x43 (2^7), so q sits in the top mantissa bits, worth 1 each.
+__device__ __forceinline__ float q128_f32(uint32_t nibbles, int k) {
+    return __uint_as_float(__byte_perm(nibbles, 0x43000000u, 0x7054u | (k << 8)));
+}
+template <int T>
+__global__ void __launch_bounds__(256) q4_gemv_kernel(const uint16_t *x, const uint32_t *w,
+                                                      const uint16_t *scales, const uint16_t *biases,
+                                                      uint16_t *y, int out_dim, int in_dim) {
+    pdl_trigger();
+    pdl_wait();
+    // shared memory: x [T][in_dim] bf16, then this CTA's 32 rows of scales and of biases
+    // ([32][groups] each, one contiguous block of the [out][groups] arrays)
+    extern __shared__ __align__(16) uint16_t gx[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rc = blockIdx.x * 8 * kGemvRows;  // first row of the CTA
+    const int r0 = rc + warp * kGemvRows;
+    const int words = in_dim / 8, groups = in_dim / kQ4Group;
+    const int runs = words / 128;
+    uint16_t *gsc = gx + T * in_dim, *gbi = gsc + 8 * kGemvRows * groups;
+    // x, scales and biases to shared memory once per CTA; the copies overlap the first batch of
+    // weight loads
+    for (int i = threadIdx.x; i < T * in_dim / 8; i += 256) cp_async16_zfill_q4(gx + 8 * i, x + 8 * i, true);
+    const int nrows = min(8 * kGemvRows, out_dim - rc);
+    for (int i = threadIdx.x; i < nrows * groups / 8; i += 256) {
+        cp_async16_zfill_q4(gsc + 8 * i, scales + (int64_t)rc * groups + 8 * i, true);
+        cp_async16_zfill_q4(gbi + 8 * i, biases + (int64_t)rc * groups + 8 * i, true);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const bool live = r0 < out_dim;
+    float acc[kGemvRows][T];
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+        for (int t = 0; t < T; ++t) acc[r][t] = 0.f;
+    // all packed words of kRuns runs in flight before any arithmetic (16 loads of 16 bytes per
+    // lane at one token): the stream is latency-bound per warp otherwise
+    constexpr int kRuns = 4;
+    uint4 wq[kRuns][kGemvRows];
+    auto load_batch = [&](int it0) {
+#pragma unroll
+        for (int j = 0; j < kRuns; ++j)
+#pragma unroll
+            for (int r = 0; r < kGemvRows; ++r)
+                if (live && it0 + j < runs)
+                    wq[j][r] = __ldcs(reinterpret_cast<const uint4 *>(w + (int64_t)(r0 + r) * words +
+                                                                       (it0 + j) * 128 + lane * 4));
+    };
+    load_batch(0);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    if (!live) return;
+    for (int it0 = 0; it0 < runs; it0 += kRuns) {
+        if (it0 > 0) load_batch(it0);
+#pragma unroll
+        for (int j = 0; j < kRuns; ++j) {
+            if (it0 + j >= runs) break;
+            const int wo = (it0 + j) * 128 + lane * 4;  // first word of this lane's half group
+            const int g = wo / 8;
+            float sc[kGemvRows], e[kGemvRows];
+#pragma unroll
+            for (int r = 0; r < kGemvRows; ++r) {
+                const int rl = warp * kGemvRows + r;
+                sc[r] = bf16_bits_to_f32(gsc[rl * groups + g]);
+                e[r] = bf16_bits_to_f32(gbi[rl * groups + g]) - 128.0f * sc[r];
+            }
+            // per (row, token): even and odd partial sums of (128 + q) x as one float2; x sums
+            float2 tmp[kGemvRows][T], xs[T];
+#pragma unroll
+            for (int t = 0; t < T; ++t) {
+                xs[t] = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int r = 0; r < kGemvRows; ++r) tmp[r][t] = make_float2(0.f, 0.f);
+            }
+#pragma unroll
+            for (int wd = 0; wd < 4; ++wd) {
+                float2 xp[T][4];  // x pairs (2k, 2k + 1) of the word's 8 inputs
+#pragma unroll
+                for (int t = 0; t < T; ++t) {
+                    const uint4 xv = *reinterpret_cast<const uint4 *>(gx + t * in_dim + (wo + wd) * 8);
+                    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        xp[t][k] = make_float2(__uint_as_float(xw[k] << 16), __uint_as_float(xw[k] & 0xFFFF0000u));
+                        xs[t] = __fadd2_rn(xs[t], xp[t][k]);
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < kGemvRows; ++r) {
+                    const uint32_t word = wd == 0 ? wq[j][r].x : wd == 1 ? wq[j][r].y : wd == 2 ? wq[j][r].z : wq[j][r].w;
+                    const uint32_t lo = word & 0x0F0F0F0Fu, hi = (word >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float2 wp = make_float2(q128_f32(lo, k), q128_f32(hi, k));
+#pragma unroll
+                        for (int t = 0; t < T; ++t) tmp[r][t] = __ffma2_rn(wp, xp[t][k], tmp[r][t]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+                for (int t = 0; t < T; ++t)
+                    acc[r][t] = fmaf(sc[r], tmp[r][t].x + tmp[r][t].y, fmaf(e[r], xs[t].x + xs[t].y, acc[r][t]));
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+            float v = acc[r][t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) y[(int64_t)t * out_dim + r0 + r] = f32_to_bf16_bits(v);
+        }
+}
+
 // ------------------------------------------------------------------ tcgen05 pieces (cta_group::1)
 __device__ __forceinline__ uint64_t q4_sdesc(uint32_t saddr) {
     // K-major operand, SWIZZLE_128B: 128-byte rows, 8-row atoms of 1024 B (SBO), version 1
@@ -583,6 +712,31 @@ extern "C" int pgc_debug_q4_trace(long long *out) {
     return cudaMemcpyFromSymbol(out, g_q4_trace, sizeof(g_q4_trace)) == cudaSuccess ? 0 : -4;
 }
 #endif
+
+cudaError_t launch_q4_gemv(const uint16_t *x, int T, const uint32_t *w, const uint16_t *scales,
+                           const uint16_t *biases, uint16_t *y, int out_dim, int in_dim, cudaStream_t stream) {
+    const dim3 grid((unsigned)((out_dim + 8 * kGemvRows - 1) / (8 * kGemvRows)));
+    const size_t smem = ((size_t)T * in_dim + 2 * 8 * kGemvRows * (in_dim / kQ4Group)) * 2;
+    static bool attr_set[64][kQ4GemvMaxTokens] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto go = [&](auto kernel) {
+        if (T < 1 || T > kQ4GemvMaxTokens) return cudaErrorInvalidValue;
+        if (dev < 0 || dev >= 64 || !attr_set[dev][T - 1]) {
+            // largest: T tokens of 8192 inputs + 2 x 32 rows of 128 groups
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (T * 8192 + 2 * 8 * kGemvRows * 128) * 2);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < 64) attr_set[dev][T - 1] = true;
+        }
+        return launch_pdl(kernel, grid, dim3(256), smem, stream, x, w, scales, biases, y, out_dim, in_dim);
+    };
+    switch (T) {
+        case 1: return go(q4_gemv_kernel<1>);
+        case 2: return go(q4_gemv_kernel<2>);
+        default: return cudaErrorInvalidValue;
+    }
+}
 
 cudaError_t q4_read_error(DevErrorHost *e, bool clear) {
     cudaError_t r = cudaMemcpyFromSymbol(e, g_q4_err, sizeof(DevError));

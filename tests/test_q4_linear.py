@@ -5,7 +5,8 @@ scale and bias), and its projection against float64 sums over the unrounded weig
 GPU: pgc_q4_dequantize bit-exact against the oracle; pgc_q4_linear against the oracle (the
 reference decode path's algebra: per group scale * sum(q x) + bias * sum(x), fp32) for the
 model's projection shapes (q|gate 4096 -> 8192, k/v 4096 -> 1024, o 4096 -> 4096), token
-counts across the 16/32/64-token tiles plus a multi-tile count, a partial 128-row tile
+counts 1-2 (the CUDA-core GEMV) and across the tcgen05 kernel's 16/32/64-token tiles plus a
+multi-tile count, a partial 128-row tile
 (out 192, 64) and in_dim 2048 and 8192 (every split-K cluster size). Tolerance for the projection: the GPU sums in the tensor
 cores' order, so |y - y_ref| <= 1 bf16 ulp of |y_ref| + 1e-3 * rms(y_ref)."""
 import numpy as np
@@ -60,7 +61,8 @@ def test_q4_dequantize_bit_exact(cuda, oracle):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("out_dim,T,in_dim", [
-    (8192, 1, 4096), (1024, 7, 4096), (1024, 16, 4096), (1024, 17, 4096), (1024, 32, 4096),
+    (8192, 1, 4096), (1024, 2, 4096), (4096, 3, 4096), (1024, 4, 8192), (64, 1, 2048),
+    (1024, 7, 4096), (1024, 16, 4096), (1024, 17, 4096), (1024, 32, 4096),
     (4096, 33, 4096), (1024, 48, 4096), (1024, 64, 4096), (1024, 130, 4096),
     (192, 5, 2048), (64, 64, 2048), (1024, 9, 8192), (4096, 64, 8192), (1024, 1000, 2048)])
 def test_q4_linear_matches_oracle(cuda, oracle, out_dim, T, in_dim):
