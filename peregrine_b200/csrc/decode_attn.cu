@@ -343,6 +343,7 @@ struct MergeParams {
     int64_t row_stride;   // floats between rows
     int64_t part_stride;  // floats between parts of a row
     int nparts;
+    int max_parts;        // upper bound of the part count (parts below it are readable)
     const int32_t *seq_lens;  // used when nparts < 0
     int rows_per_seq;
     int tokens_per_split;
@@ -352,6 +353,8 @@ struct MergeParams {
 };
 
 constexpr int kMergeWarps = 8;
+
+constexpr int kMergeCached = 10;  // parts per warp held in registers: rows of up to 80 parts
 
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergeParams p) {
     pdl_trigger();
@@ -363,29 +366,68 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int d = blockIdx.y * 32 + lane;
-    int np = p.nparts;
-    if (np < 0) {
-        const int L = p.seq_lens[row / p.rows_per_seq];
-        np = (L + p.tokens_per_split - 1) / p.tokens_per_split;
-    }
     const float *base = p.parts + row * p.row_stride;
     float ma = -INFINITY;
-    for (int c = threadIdx.x; c < np; c += kMergeWarps * 32) ma = fmaxf(ma, base[c * p.part_stride]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
-    if (lane == 0) red_m[warp] = ma;
-    __syncthreads();
-    ma = red_m[0];
-#pragma unroll
-    for (int w = 1; w < kMergeWarps; ++w) ma = fmaxf(ma, red_m[w]);
     float den = 0.f, acc = 0.f;
+    if (p.max_parts <= kMergeWarps * kMergeCached) {
+        // one round of loads after the part count: every (m, l, o[d]) of this warp's parts, then
+        // the maximum, the weights and the sums from registers
+        int np = p.nparts;
+        if (np < 0) {
+            const int L = p.seq_lens[row / p.rows_per_seq];
+            np = (L + p.tokens_per_split - 1) / p.tokens_per_split;
+        }
+        float mc[kMergeCached], lc[kMergeCached], oc[kMergeCached];
+#pragma unroll
+        for (int i = 0; i < kMergeCached; ++i) {
+            const int c = warp + kMergeWarps * i;
+            mc[i] = -INFINITY;
+            lc[i] = oc[i] = 0.f;
+            if (c < np) {
+                const float *pc = base + c * p.part_stride;
+                mc[i] = pc[0];
+                lc[i] = pc[1];
+                oc[i] = pc[2 + d];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kMergeCached; ++i)
+            if (warp + kMergeWarps * i < np) ma = fmaxf(ma, mc[i]);
+        if (lane == 0) red_m[warp] = ma;  // m is the same in every lane of the warp
+        __syncthreads();
+        ma = red_m[0];
+#pragma unroll
+        for (int w = 1; w < kMergeWarps; ++w) ma = fmaxf(ma, red_m[w]);
+#pragma unroll
+        for (int i = 0; i < kMergeCached; ++i) {
+            if (warp + kMergeWarps * i < np && mc[i] != -INFINITY) {
+                const float w = exp2f((mc[i] - ma) * kLog2e);
+                den += lc[i] * w;
+                acc += oc[i] * w;
+            }
+        }
+    } else {
+        int np = p.nparts;
+        if (np < 0) {
+            const int L = p.seq_lens[row / p.rows_per_seq];
+            np = (L + p.tokens_per_split - 1) / p.tokens_per_split;
+        }
+        for (int c = threadIdx.x; c < np; c += kMergeWarps * 32) ma = fmaxf(ma, base[c * p.part_stride]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+        if (lane == 0) red_m[warp] = ma;
+        __syncthreads();
+        ma = red_m[0];
+#pragma unroll
+        for (int w = 1; w < kMergeWarps; ++w) ma = fmaxf(ma, red_m[w]);
 #pragma unroll 4
-    for (int c = warp; c < np; c += kMergeWarps) {
-        const float *pc = base + c * p.part_stride;
-        const float mc = pc[0];
-        const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - ma) * kLog2e);
-        den += pc[1] * w;
-        acc += pc[2 + d] * w;
+        for (int c = warp; c < np; c += kMergeWarps) {
+            const float *pc = base + c * p.part_stride;
+            const float mcv = pc[0];
+            const float w = (mcv == -INFINITY) ? 0.f : exp2f((mcv - ma) * kLog2e);
+            den += pc[1] * w;
+            acc += pc[2 + d] * w;
+        }
     }
     red_acc[warp][lane] = acc;
     if (lane == 0) red_den[warp] = den;
@@ -530,6 +572,7 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
     mp.row_stride = (int64_t)plan.max_splits * kPartial;
     mp.part_stride = kPartial;
     mp.nparts = -1;
+    mp.max_parts = plan.max_splits;
     mp.seq_lens = seq_lens;
     mp.rows_per_seq = num_queries * kNumQHeads;
     mp.tokens_per_split = plan.pages_per_split * kPage;
@@ -549,6 +592,7 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
     mp.row_stride = kPartial;
     mp.part_stride = part_stride;
     mp.nparts = num_parts;
+    mp.max_parts = num_parts;
     mp.seq_lens = nullptr;
     mp.rows_per_seq = 1;
     mp.tokens_per_split = 1;
