@@ -132,3 +132,35 @@ def test_host_validation(cuda):
         cuda.decode_attn(z, pool, pool, tbl, sl, 10, SCALE, out, ws, num_queries=5)
     with pytest.raises(PgcError, match="ALIGN"):
         cuda.decode_attn(z[1:], pool, pool, tbl, sl, 10, SCALE, out, ws)
+
+
+def test_single_long_sequence_merge_over_80_parts(cuda, oracle):
+    """One 100000-token sequence: 98 key-range splits, more than the merge keeps in registers
+    (80 per row), so the merge takes its streaming path."""
+    lens = [100000]
+    q, kp, vp, table, seq, g = _case(oracle, lens, seed=11, gate=True, spare_pages=0)
+    got = _run(cuda, q, kp, vp, table, seq, 1, g)
+    ref, _ = oracle.decode_paged(q, kp, vp, table, seq, SCALE, 1, g)
+    assert_attn_close(got, ref)
+
+
+@pytest.mark.parametrize("num_parts", [20, 80, 81, 130])
+def test_merge_partials_part_counts(cuda, oracle, num_parts):
+    """pgc_merge_partials across the merge's register path (up to 80 parts per row) and its
+    streaming path, with empty parts (m = -inf, l = 0, o = 0) mixed in."""
+    import torch
+    rng = np.random.default_rng(num_parts)
+    rows = 16
+    parts = np.zeros((num_parts, rows, 258), np.float32)
+    parts[:, :, 0] = rng.standard_normal((num_parts, rows)) * 3.0
+    parts[:, :, 1] = rng.random((num_parts, rows)) * 50.0 + 1.0
+    parts[:, :, 2:] = rng.standard_normal((num_parts, rows, 256)) * parts[:, :, 1:2]
+    empty = rng.random((num_parts, rows)) < 0.2
+    parts[empty, 0] = -np.inf
+    parts[empty, 1:] = 0.0
+    g = oracle.normal_bf16(rows * D, 3).reshape(rows, D)
+    ref, _ = oracle.merge_partials(parts, rows, num_parts, rows * 258, g)
+    out = torch.empty((rows, D), dtype=torch.int16, device="cuda")
+    cuda.merge_partials(torch.from_numpy(parts).cuda(), rows, num_parts, rows * 258, out, gate=dev(g))
+    torch.cuda.synchronize()
+    assert_attn_close(host_u16(out).reshape(1, 1, rows, D), ref.reshape(1, 1, rows, D))
