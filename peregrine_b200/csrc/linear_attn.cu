@@ -350,12 +350,6 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
-__device__ __forceinline__ void fma4(float (&acc)[4], float a, const float4 &b) {
-    acc[0] = fmaf(a, b.x, acc[0]);
-    acc[1] = fmaf(a, b.y, acc[1]);
-    acc[2] = fmaf(a, b.z, acc[2]);
-    acc[3] = fmaf(a, b.w, acc[3]);
-}
 __device__ __forceinline__ float dot4(const float4 &a, const float4 &b, float acc) {
     acc = fmaf(a.x, b.x, acc);
     acc = fmaf(a.y, b.y, acc);
@@ -493,13 +487,66 @@ __global__ void __launch_bounds__(256, 2) gated_delta_chunk_kernel(const float *
     for (int i = 0; i < kChunk; ++i) dst[i * kDk + col] = us[i * kDk + col];
 }
 
+// 3xTF32 products on the tensor cores (mma.sync m16n8k8): each fp32 operand x is split into
+// big = tf32(x) and small = tf32(x - big), and a*b is accumulated as a_small*b_big +
+// a_big*b_small + a_big*b_big, which keeps about 22 bits of every product (the small*small term
+// is below fp32 rounding).
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t &big, uint32_t &small) {
+    big = tf32_rna(x);
+    small = tf32_rna(x - __uint_as_float(big));
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// A fragment (16 x 8, row-major) of rows r0 + g and r0 + g + 8, columns c + t and c + t + 4,
+// read from f32 rows of `ld` floats, split into big and small parts
+__device__ __forceinline__ void frag_a(const float *m, int ld, int r0, int c, int g, int t, uint32_t (&big)[4],
+                                       uint32_t (&small)[4]) {
+    split_tf32(m[(r0 + g) * ld + c + t], big[0], small[0]);
+    split_tf32(m[(r0 + g + 8) * ld + c + t], big[1], small[1]);
+    split_tf32(m[(r0 + g) * ld + c + t + 4], big[2], small[2]);
+    split_tf32(m[(r0 + g + 8) * ld + c + t + 4], big[3], small[3]);
+}
+__device__ __forceinline__ void mma3(float (&d)[4], const uint32_t (&ab)[4], const uint32_t (&as)[4], uint32_t bb0,
+                                     uint32_t bb1, uint32_t bs0, uint32_t bs1) {
+    mma_tf32(d, as, bb0, bb1);
+    mma_tf32(d, ab, bs0, bs1);
+    mma_tf32(d, ab, bb0, bb1);
+}
+
 // The state walk: CTA = (32 value rows, value head), 256 threads; the 32 x 128 state slice stays
 // in shared memory across chunks. Each chunk's tiles are staged in shared memory with cp.async
 // in two groups, A = {W, Q, U slice} and B = {K, QKm, lg}: A of chunk c+1 loads during phase 2
 // of chunk c (after phase 1 has released W, Q, U), B of chunk c+1 during phase 1 of chunk c+1.
-//   phase 1   delta = U - W S^T, QS = Q S^T       thread: rows i = 2ty, 2ty+1; value rows tx + 8m
-//   phase 2a  y = e^{lg} QS + QKm delta           same mapping, from registers
-//   phase 2b  S = e^{lg_C} S + (e^{lg_C - lg} delta)^T K   thread: value rows 4tx.., keys 4ty..
+// The three products run on the tensor cores in 3xTF32 (g = lane / 4, t = lane % 4 below):
+//   phase 1   delta = U - W S^T, QS = Q S^T    warp w: rows 16 (w / 2).., value rows 16 (w % 2)..
+//   phase 2a  y = e^{lg} QS + QKm delta        same tile (QS stays in registers)
+//   phase 2b  S = e^{lg_C} S + (e^{lg_C - lg} delta)^T K   warp w: value rows 16 (w / 4)..,
+//                                                           keys 32 (w % 4)..
+// Shared-memory rows are padded to 4 mod 32 floats, so every fragment read is conflict-free.
+#ifdef PGC_LIN_TRACE
+// Diagnostic build only: clock64 at the scan's phase boundaries, CTA (0, 0), chunk j < 64.
+static __device__ long long g_lin_trace[6][64];
+#define LIN_TRACE(ev, j)                                                                      \
+    do {                                                                                      \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && (j) < 64)              \
+            g_lin_trace[ev][j] = clock64();                                                   \
+    } while (0)
+#else
+#define LIN_TRACE(ev, j) \
+    do {                 \
+    } while (0)
+#endif
+
 constexpr int kRowsScan = 32;
 constexpr int kDP = kRowsScan + 4;
 struct ScanSmem {
@@ -507,8 +554,8 @@ struct ScanSmem {
     static constexpr int W = S + kRowsScan * kRowP;          // [64][132]
     static constexpr int Q = W + kChunk * kRowP;             // [64][132]
     static constexpr int U = Q + kChunk * kRowP;             // [64][32]
-    static constexpr int K = U + kChunk * kRowsScan;         // [64][128]
-    static constexpr int QK = K + kChunk * kDk;              // [64][68]
+    static constexpr int K = U + kChunk * kRowsScan;         // [64][132]
+    static constexpr int QK = K + kChunk * kRowP;            // [64][68]
     static constexpr int LG = QK + kChunk * kQKP;            // [64]
     static constexpr int D = LG + kChunk;                    // [64][36]
     static constexpr int Ds = D + kChunk * kDP;              // [64][36], scaled by e^{lg_C - lg}
@@ -525,7 +572,7 @@ __global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *stat
     float *S = cs_smem + ScanSmem::S, *Ws = cs_smem + ScanSmem::W, *Qs = cs_smem + ScanSmem::Q;
     float *Us = cs_smem + ScanSmem::U, *Ks = cs_smem + ScanSmem::K, *QKs = cs_smem + ScanSmem::QK;
     float *LGs = cs_smem + ScanSmem::LG, *Dl = cs_smem + ScanSmem::D, *Dsc = cs_smem + ScanSmem::Ds;
-    const int tid = threadIdx.x, tx = tid & 7, ty = tid >> 3;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
     const int hv = blockIdx.y, hk = hv / (kHv / kHk);
     const int r0 = blockIdx.x * kRowsScan;
     const int nc = (T + kChunk - 1) / kChunk;
@@ -556,7 +603,7 @@ __global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *stat
         for (int i = tid; i < kChunk * kDk / 4; i += 256) {
             const int r = i >> 5, k4 = i & 31;
             const bool ok = r < n;
-            cp_async16_zfill(Ks + r * kDk + 4 * k4, ok ? Kg + r * kDk + 4 * k4 : Kg, ok);
+            cp_async16_zfill(Ks + r * kRowP + 4 * k4, ok ? Kg + r * kDk + 4 * k4 : Kg, ok);
         }
         for (int i = tid; i < kChunk * kChunk / 4; i += 256) {
             const int r = i >> 4, q = i & 15;
@@ -570,37 +617,46 @@ __global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *stat
     issue_b(0);
     for (int i = tid; i < kRowsScan * kDk; i += 256)
         S[(i / kDk) * kRowP + i % kDk] = has_state ? st_g[i] : 0.f;
+    const int i0 = (w >> 1) * 16, n0 = (w & 1) * 16;  // phase 1 / 2a tile
+    const int rb = (w >> 2) * 16, kb = (w & 3) * 32;   // phase 2b tile
     for (int c = 0; c < nc; ++c) {
         const int t0 = c * kChunk, n = min(kChunk, T - t0);
+        LIN_TRACE(0, c);
         cp_async_wait<1>();  // A(c) landed (B(c) may still be in flight)
         __syncthreads();
-        // phase 1
-        float d[2][4] = {}, qs[2][4] = {};
-        {
-            const float *w0 = Ws + (2 * ty) * kRowP, *w1 = w0 + kRowP;
-            const float *q0 = Qs + (2 * ty) * kRowP, *q1 = q0 + kRowP;
-#pragma unroll 4
-            for (int k = 0; k < kDk; k += 4) {
-                const float4 a0 = ld4(w0 + k), a1 = ld4(w1 + k), b0 = ld4(q0 + k), b1 = ld4(q1 + k);
+        LIN_TRACE(1, c);
+        // phase 1: dacc = W S^T, qacc = Q S^T over the 128 keys
+        float dacc[2][4] = {}, qacc[2][4] = {};
+#pragma unroll 2
+        for (int k = 0; k < kDk; k += 8) {
+            uint32_t wb[4], wsm[4], qb[4], qsm[4];
+            frag_a(Ws, kRowP, i0, k, g, t, wb, wsm);
+            frag_a(Qs, kRowP, i0, k, g, t, qb, qsm);
 #pragma unroll
-                for (int m = 0; m < 4; ++m) {
-                    const float4 sv = ld4(S + (tx + 8 * m) * kRowP + k);
-                    d[0][m] = dot4(a0, sv, d[0][m]);
-                    d[1][m] = dot4(a1, sv, d[1][m]);
-                    qs[0][m] = dot4(b0, sv, qs[0][m]);
-                    qs[1][m] = dot4(b1, sv, qs[1][m]);
-                }
+            for (int nn = 0; nn < 2; ++nn) {
+                // B[k][r] = S[r][k]: column r = n0 + 8 nn + g, rows k + t and k + t + 4
+                const float *sr = S + (n0 + 8 * nn + g) * kRowP + k + t;
+                uint32_t bb0, bs0, bb1, bs1;
+                split_tf32(sr[0], bb0, bs0);
+                split_tf32(sr[4], bb1, bs1);
+                mma3(dacc[nn], wb, wsm, bb0, bb1, bs0, bs1);
+                mma3(qacc[nn], qb, qsm, bb0, bb1, bs0, bs1);
             }
-#pragma unroll
-            for (int x = 0; x < 2; ++x)
-#pragma unroll
-                for (int m = 0; m < 4; ++m) {
-                    const int i = 2 * ty + x, r = tx + 8 * m;
-                    d[x][m] = Us[i * kRowsScan + r] - d[x][m];
-                    Dl[i * kDP + r] = d[x][m];
-                }
         }
-        __syncthreads();  // W, Q, U released; D complete
+        // delta = U - W S^T at rows i0 + g (+8), value rows n0 + 8 nn + 2t (+1)
+#pragma unroll
+        for (int nn = 0; nn < 2; ++nn) {
+            const int col = n0 + 8 * nn + 2 * t;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int i = i0 + g + 8 * h;
+                dacc[nn][2 * h] = Us[i * kRowsScan + col] - dacc[nn][2 * h];
+                dacc[nn][2 * h + 1] = Us[i * kRowsScan + col + 1] - dacc[nn][2 * h + 1];
+                *reinterpret_cast<float2 *>(Dl + i * kDP + col) = make_float2(dacc[nn][2 * h], dacc[nn][2 * h + 1]);
+            }
+        }
+        LIN_TRACE(2, c);
+        __syncthreads();  // W, Q, U released; delta complete
         if (c + 1 < nc) {
             issue_a(c + 1);
             cp_async_wait<1>();  // B(c)
@@ -608,60 +664,94 @@ __global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *stat
             cp_async_wait<0>();
         }
         __syncthreads();
+        LIN_TRACE(3, c);
         const float lgC = LGs[n - 1];
-        // phase 2a and the scaled copy of delta
+        // phase 2a: y = e^{lg} QS + QKm delta (QKm is zero above the diagonal: j <= i0 + 15)
+        {
+            float yacc[2][4];
+            const float e0 = expf(LGs[i0 + g]), e1 = expf(LGs[i0 + g + 8]);
+            const float c0 = expf(lgC - LGs[i0 + g]), c1 = expf(lgC - LGs[i0 + g + 8]);
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-            const int i = 2 * ty + x;
-            const float li = LGs[i];
-            const float ei = expf(li), ec = expf(lgC - li);
-            float acc[4];
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                acc[m] = ei * qs[x][m];
-                Dsc[i * kDP + tx + 8 * m] = d[x][m] * ec;
+            for (int nn = 0; nn < 2; ++nn) {
+                yacc[nn][0] = e0 * qacc[nn][0];
+                yacc[nn][1] = e0 * qacc[nn][1];
+                yacc[nn][2] = e1 * qacc[nn][2];
+                yacc[nn][3] = e1 * qacc[nn][3];
+                const int col = n0 + 8 * nn + 2 * t;
+                *reinterpret_cast<float2 *>(Dsc + (i0 + g) * kDP + col) =
+                    make_float2(dacc[nn][0] * c0, dacc[nn][1] * c0);
+                *reinterpret_cast<float2 *>(Dsc + (i0 + g + 8) * kDP + col) =
+                    make_float2(dacc[nn][2] * c1, dacc[nn][3] * c1);
             }
-            for (int j = 0; j <= i; ++j) {
-                const float a = QKs[i * kQKP + j];
+            for (int j = 0; j < i0 + 16; j += 8) {
+                uint32_t ab[4], as[4];
+                frag_a(QKs, kQKP, i0, j, g, t, ab, as);
 #pragma unroll
-                for (int m = 0; m < 4; ++m) acc[m] = fmaf(a, Dl[j * kDP + tx + 8 * m], acc[m]);
+                for (int nn = 0; nn < 2; ++nn) {
+                    // B[j][r] = delta[j][r]: column n0 + 8 nn + g, rows j + t and j + t + 4
+                    const float *dr = Dl + (j + t) * kDP + n0 + 8 * nn + g;
+                    uint32_t bb0, bs0, bb1, bs1;
+                    split_tf32(dr[0], bb0, bs0);
+                    split_tf32(dr[4 * kDP], bb1, bs1);
+                    mma3(yacc[nn], ab, as, bb0, bb1, bs0, bs1);
+                }
             }
-            if (i < n) {
 #pragma unroll
-                for (int m = 0; m < 4; ++m)
-                    y[(int64_t)(t0 + i) * kValDim + hv * kDv + r0 + tx + 8 * m] = f32_to_bf16_bits(acc[m]);
+            for (int nn = 0; nn < 2; ++nn) {
+                const int col = r0 + n0 + 8 * nn + 2 * t;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int i = i0 + g + 8 * h;
+                    if (i < n)
+                        *reinterpret_cast<uint32_t *>(y + (int64_t)(t0 + i) * kValDim + hv * kDv + col) =
+                            pack_bf16x2(yacc[nn][2 * h], yacc[nn][2 * h + 1]);
+                }
             }
         }
-        __syncthreads();  // Dsc complete
-        // phase 2b: this thread's 4 value rows x 4 keys of S
+        LIN_TRACE(4, c);
+        __syncthreads();  // the scaled delta is complete
+        // phase 2b: S[r][k] = e^{lg_C} S[r][k] + sum_j Dsc[j][r] K[j][k] for this warp's tile
         {
             const float eC = expf(lgC);
             float sacc[4][4];
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                const float4 sv = ld4(S + (4 * tx + m) * kRowP + 4 * ty);
-                sacc[m][0] = eC * sv.x;
-                sacc[m][1] = eC * sv.y;
-                sacc[m][2] = eC * sv.z;
-                sacc[m][3] = eC * sv.w;
+            for (int nn = 0; nn < 4; ++nn) {
+                const int col = kb + 8 * nn + 2 * t;
+                const float2 s0 = *reinterpret_cast<const float2 *>(S + (rb + g) * kRowP + col);
+                const float2 s1 = *reinterpret_cast<const float2 *>(S + (rb + g + 8) * kRowP + col);
+                sacc[nn][0] = eC * s0.x;
+                sacc[nn][1] = eC * s0.y;
+                sacc[nn][2] = eC * s1.x;
+                sacc[nn][3] = eC * s1.y;
             }
-#pragma unroll 8
-            for (int j = 0; j < kChunk; ++j) {
-                const float4 dj = ld4(Dsc + j * kDP + 4 * tx);
-                const float4 kj = ld4(Ks + j * kDk + 4 * ty);
-                fma4(sacc[0], dj.x, kj);
-                fma4(sacc[1], dj.y, kj);
-                fma4(sacc[2], dj.z, kj);
-                fma4(sacc[3], dj.w, kj);
-            }
-            // S is read by other threads only in phase 1, which every thread has finished; each
-            // element here has exactly one owner.
+#pragma unroll 2
+            for (int j = 0; j < kChunk; j += 8) {
+                // A[r][j] = Dsc[j][r]: rows rb + g (+8), columns j + t (+4)
+                uint32_t ab[4], as[4];
+                split_tf32(Dsc[(j + t) * kDP + rb + g], ab[0], as[0]);
+                split_tf32(Dsc[(j + t) * kDP + rb + g + 8], ab[1], as[1]);
+                split_tf32(Dsc[(j + t + 4) * kDP + rb + g], ab[2], as[2]);
+                split_tf32(Dsc[(j + t + 4) * kDP + rb + g + 8], ab[3], as[3]);
 #pragma unroll
-            for (int m = 0; m < 4; ++m)
-                *reinterpret_cast<float4 *>(S + (4 * tx + m) * kRowP + 4 * ty) =
-                    make_float4(sacc[m][0], sacc[m][1], sacc[m][2], sacc[m][3]);
+                for (int nn = 0; nn < 4; ++nn) {
+                    const float *kr = Ks + (j + t) * kRowP + kb + 8 * nn + g;
+                    uint32_t bb0, bs0, bb1, bs1;
+                    split_tf32(kr[0], bb0, bs0);
+                    split_tf32(kr[4 * kRowP], bb1, bs1);
+                    mma3(sacc[nn], ab, as, bb0, bb1, bs0, bs1);
+                }
+            }
+            // every thread has finished reading S (phase 1) before this point; each element
+            // below has one owner
+#pragma unroll
+            for (int nn = 0; nn < 4; ++nn) {
+                const int col = kb + 8 * nn + 2 * t;
+                *reinterpret_cast<float2 *>(S + (rb + g) * kRowP + col) = make_float2(sacc[nn][0], sacc[nn][1]);
+                *reinterpret_cast<float2 *>(S + (rb + g + 8) * kRowP + col) = make_float2(sacc[nn][2], sacc[nn][3]);
+            }
         }
-        __syncthreads();  // K, QKm, lg, D released
+        LIN_TRACE(5, c);
+        __syncthreads();  // K, QKm, lg, delta released
         if (c + 1 < nc) issue_b(c + 1);
     }
     __syncthreads();
@@ -730,6 +820,12 @@ cudaError_t launch_gated_delta_prefill(float *state, int has_state, const uint16
     return launch_pdl(gated_delta_chunk_scan_kernel, dim3(kDv / kRowsScan, kHv), dim3(256), kScanSmemC, stream,
                       state, has_state, (const float *)qn, (const float *)kn, (const float *)cw, T, y);
 }
+
+#ifdef PGC_LIN_TRACE
+extern "C" int pgc_debug_lin_trace2(long long *out) {
+    return cudaMemcpyFromSymbol(out, g_lin_trace, sizeof(g_lin_trace)) == cudaSuccess ? 0 : -4;
+}
+#endif
 
 cudaError_t linear_read_error(DevErrorHost *e, bool clear) {
     cudaError_t r = cudaMemcpyFromSymbol(e, g_linear_err, sizeof(DevError));
