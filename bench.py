@@ -262,33 +262,45 @@ def bench_config1(capi, iters=20):
     seq = torch.tensor([L + 1], dtype=torch.int32, device="cuda")
     ws = torch.empty(capi.decode_workspace_bytes(1, 1, L + 1), dtype=torch.uint8, device="cuda")
 
-    def step(st, c):
+    def fused_step(st, c):
+        capi.decode_attn_append(q_in, k_in, v_in, rope, pos, slot, kps[c], vps[c], table, seq, L + 1,
+                                SCALE, out, ws, stream=st)
+
+    def two_call_step(st, c):
         capi.append_kv_rope(q_in, q, k_in, v_in, rope, pos, slot, kps[c], vps[c], stream=st)
         capi.decode_attn(q, kps[c], vps[c], table, seq, L + 1, SCALE, out, ws, stream=st)
 
-    def all_copies(st):
-        for c in range(copies):
-            step(st, c)
-
     s = torch.cuda.current_stream()
-    direct = _ev_time(lambda: all_copies(s), iters) / copies
-    graph_ms = None
-    try:
-        gr = torch.cuda.CUDAGraph()
-        cap = torch.cuda.Stream()
-        cap.wait_stream(s)
-        with torch.cuda.graph(gr, stream=cap):
-            all_copies(cap)
-        s.wait_stream(cap)
-        graph_ms = _ev_time(gr.replay, iters) / copies
-    except Exception as e:  # the graph figure is optional
-        print(f"config1 graph capture failed: {e}", file=sys.stderr)
+
+    def timed(step):
+        def all_copies(st):
+            for c in range(copies):
+                step(st, c)
+        direct = _ev_time(lambda: all_copies(s), iters) / copies
+        graph_ms = None
+        try:
+            gr = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream()
+            cap.wait_stream(s)
+            with torch.cuda.graph(gr, stream=cap):
+                all_copies(cap)
+            s.wait_stream(cap)
+            graph_ms = _ev_time(gr.replay, iters) / copies
+        except Exception as e:  # the graph figure is optional
+            print(f"config1 graph capture failed: {e}", file=sys.stderr)
+        return direct, graph_ms
+
+    direct, graph_ms = timed(fused_step)
+    direct2, graph2 = timed(two_call_step)
     nbytes = (L + 1) * KV_BYTES_PER_TOKEN + 3 * NQ * D * 2 + 2 * NKV * D * 2
     best = direct if graph_ms is None else min(direct, graph_ms)
-    return {"workload": "config1: 1 layer, 4097-token decode + 1 append at pos 4096 (16 cache copies "
-                        "in rotation: K/V read from HBM, not L2)",
+    return {"workload": "config1: 1 layer, 4097-token decode + 1 append at pos 4096, fused in one "
+                        "launch (pgc_decode_attn_append); 16 cache copies in rotation: K/V read from "
+                        "HBM, not L2",
             "us_per_step": round(direct * 1e3, 2),
             "us_per_step_graph": None if graph_ms is None else round(graph_ms * 1e3, 2),
+            "us_per_step_two_calls": round(direct2 * 1e3, 2),
+            "us_per_step_graph_two_calls": None if graph2 is None else round(graph2 * 1e3, 2),
             "GB_s": round(nbytes / (best * 1e-3) / 1e9, 1), "algorithmic_bytes": nbytes}
 
 
@@ -431,56 +443,68 @@ def bench_config3(capi, iters=10):
     s = torch.cuda.current_stream()
     counter = {"i": 0}
 
+    def layer_ops(st, fused):
+        for l in range(layers):
+            if fused:
+                capi.decode_attn_append(q_in[l], k_in[l], v_in[l], rope, pos, slots, kp[l], vp[l], table,
+                                        seq, L + 2, SCALE, out, ws, num_queries=2, q_norm_w=qw, k_norm_w=kw,
+                                        stream=st)
+            else:
+                capi.append_kv_rope(q_in[l], q, k_in[l], v_in[l], rope, pos, slots, kp[l], vp[l],
+                                    gate_out=gate, q_norm_w=qw, k_norm_w=kw, stream=st)
+                capi.decode_attn(q, kp[l], vp[l], table, seq, L + 2, SCALE, out, ws, num_queries=2,
+                                 gate=gate, stream=st)
+
     def step():
         i = counter["i"] % len(flags)
         counter["i"] += 1
         seq.fill_(L + 2)
         capi.copy_regions(snap_regions, stream=s)
-        for l in range(layers):
-            capi.append_kv_rope(q_in[l], q, k_in[l], v_in[l], rope, pos, slots, kp[l], vp[l],
-                                gate_out=gate, q_norm_w=qw, k_norm_w=kw, stream=s)
-            capi.decode_attn(q, kp[l], vp[l], table, seq, L + 2, SCALE, out, ws, num_queries=2,
-                             gate=gate, stream=s)
+        layer_ops(s, True)
         capi.rollback(accept[i:i + 1], seq, 0, 1, back_regions, stream=s)
 
     ms_direct = _ev_time(step, iters)
     # the same step as one CUDA graph (launch overhead removed); the acceptance flag of each
-    # replay is copied into the captured flag buffer first
+    # replay is copied into the captured flag buffer first. The two-call form (append, then
+    # decode) is timed the same way for comparison.
     acc = torch.zeros(1, dtype=torch.int32, device="cuda")
-    ms_graph = None
-    try:
-        gr = torch.cuda.CUDAGraph()
-        cap = torch.cuda.Stream()
-        cap.wait_stream(s)
-        with torch.cuda.graph(gr, stream=cap):
-            seq.fill_(L + 2)
-            capi.copy_regions(snap_regions, stream=cap)
-            for l in range(layers):
-                capi.append_kv_rope(q_in[l], q, k_in[l], v_in[l], rope, pos, slots, kp[l], vp[l],
-                                    gate_out=gate, q_norm_w=qw, k_norm_w=kw, stream=cap)
-                capi.decode_attn(q, kp[l], vp[l], table, seq, L + 2, SCALE, out, ws,
-                                 num_queries=2, gate=gate, stream=cap)
-            capi.rollback(acc, seq, 0, 1, back_regions, stream=cap)
-        s.wait_stream(cap)
 
-        def replay():
-            i = counter["i"] % len(flags)
-            counter["i"] += 1
-            acc.copy_(accept[i:i + 1])
-            gr.replay()
+    def graph_ms(fused):
+        try:
+            gr = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream()
+            cap.wait_stream(s)
+            with torch.cuda.graph(gr, stream=cap):
+                seq.fill_(L + 2)
+                capi.copy_regions(snap_regions, stream=cap)
+                layer_ops(cap, fused)
+                capi.rollback(acc, seq, 0, 1, back_regions, stream=cap)
+            s.wait_stream(cap)
 
-        ms_graph = _ev_time(replay, iters)
-    except Exception as e:
-        print(f"config3 graph capture failed: {e}", file=sys.stderr)
+            def replay():
+                i = counter["i"] % len(flags)
+                counter["i"] += 1
+                acc.copy_(accept[i:i + 1])
+                gr.replay()
+
+            return _ev_time(replay, iters)
+        except Exception as e:
+            print(f"config3 graph capture failed: {e}", file=sys.stderr)
+            return None
+
+    ms_graph = graph_ms(True)
+    ms_two = graph_ms(False)
     ms = ms_direct if ms_graph is None else min(ms_direct, ms_graph)
     kv = layers * (L + 2) * KV_BYTES_PER_TOKEN
     state = sum(nb)
     reject_rate = 1.0 - float(flags.mean())
     moved = kv + 2 * state + reject_rate * 2 * state  # KV read, snapshot r+w, expected restore r+w
-    return {"workload": "config3: MTP verify, 2 queries over 32768 tokens x 8 layers, state "
-                        "snapshot + device-side Bernoulli(0.7) rollback",
+    return {"workload": "config3: MTP verify, 2 queries over 32768 tokens x 8 layers (append fused "
+                        "into the decode, pgc_decode_attn_append), state snapshot + device-side "
+                        "Bernoulli(0.7) rollback",
             "ms_per_verify": round(ms, 3), "ms_per_verify_direct": round(ms_direct, 3),
             "ms_per_verify_graph": None if ms_graph is None else round(ms_graph, 3),
+            "ms_per_verify_graph_two_calls": None if ms_two is None else round(ms_two, 3),
             "kv_bytes": kv, "state_bytes": state,
             "GB_s": round(moved / (ms * 1e-3) / 1e9, 1)}
 

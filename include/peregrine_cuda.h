@@ -168,6 +168,22 @@ int pgc_decode_attn_partials(const uint16_t *q, const uint16_t *k_pages,
 /* Size of the fixed scratch array behind pgc_decode_attn_static (16 MiB per GPU). */
 #define PGC_DECODE_STATIC_SCRATCH_BYTES (16u << 20)
 
+/* block_attn.zig:322-356 in one launch: pgc_append_kv_rope in decode mode (RMSNorm + RoPE of the
+ * q and k heads, the new K/V rows written at slot_mapping) fused into pgc_decode_attn, the same
+ * bits as the two calls in sequence. q_in [batch * num_queries][16][q_head_stride] bf16, either q
+ * (256) or the packed q | gate rows (512: the gate gates the output as in pgc_decode_attn); k_in,
+ * v_in [batch * num_queries][4][256]; token t = seq * num_queries + j at positions[t] (the last
+ * num_queries tokens of its sequence, counted in seq_lens). The rotated q is not written out.
+ * Position and slot errors are recorded in the decode unit of pgc_device_error. */
+int pgc_decode_attn_append(const uint16_t *q_in, int q_head_stride, const uint16_t *k_in,
+                           const uint16_t *v_in, const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                           const float *rope_table, int64_t rope_max_pos, const int32_t *positions,
+                           const int64_t *slot_mapping, uint16_t *k_pages, uint16_t *v_pages,
+                           int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
+                           const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
+                           float scale, uint16_t *out, void *workspace, size_t workspace_bytes,
+                           void *stream);
+
 /* pgc_decode_attn without a caller workspace, for callers that cannot allocate device memory
  * at all: code running where cudaMalloc is unavailable or forbidden (a host whose allocator
  * owns all device memory, a real-time serving loop that bans allocation after start-up, a

@@ -103,6 +103,8 @@ SIGNATURES = {
     "pgc_decode_workspace_bytes": (SZ, [I32, I32, I32]),
     "pgc_decode_attn": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, P, SZ, P]),
     "pgc_decode_attn_static": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, P]),
+    "pgc_decode_attn_append": (I32, [P, I32, P, P, P, P, P, I64, P, P, P, P, I64, P, I32, P, I32, I32, I32,
+                                     F32, P, P, SZ, P]),
     "pgc_decode_attn_partials": (I32, [P, P, P, I64, P, I32, P, I32, I32, I32, F32, P, P, SZ, P]),
     "pgc_merge_partials": (I32, [P, I64, I32, I64, P, P, P]),
     "pgc_prefill_workspace_bytes": (SZ, [I32, I32]),
@@ -242,6 +244,20 @@ def decode_attn(q, k_pages, v_pages, block_tables, seq_lens, max_seq_len, scale,
         block_tables.shape[1], _ptr(seq_lens), batch, num_queries, max_seq_len, scale, _ptr(gate),
         _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(stream)),
         "pgc_decode_attn")
+
+
+def decode_attn_append(q_in, k_in, v_in, rope, positions, slots, k_pages, v_pages, block_tables,
+                       seq_lens, max_seq_len, scale, out, workspace, num_queries=1, q_norm_w=None,
+                       k_norm_w=None, stream=None) -> None:
+    """pgc_decode_attn_append: the decode append (RMSNorm + RoPE, new K/V rows into the pool) and
+    the attention in one launch. q_in [tokens][16][256 or 512 (q | gate)]."""
+    batch = seq_lens.shape[0]
+    check(lib().pgc_decode_attn_append(
+        _ptr(q_in), q_in.shape[-1], _ptr(k_in), _ptr(v_in), _ptr(q_norm_w), _ptr(k_norm_w), _ptr(rope),
+        rope.shape[0], _ptr(positions), _ptr(slots), _ptr(k_pages), _ptr(v_pages), k_pages.shape[0],
+        _ptr(block_tables), block_tables.shape[1], _ptr(seq_lens), batch, num_queries, max_seq_len,
+        scale, _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(stream)),
+        "pgc_decode_attn_append")
 
 
 def decode_attn_static(q, k_pages, v_pages, block_tables, seq_lens, max_seq_len, scale, out,

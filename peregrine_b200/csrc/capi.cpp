@@ -328,6 +328,46 @@ int pgc_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *
                                      static_cast<cudaStream_t>(stream)));
 }
 
+int pgc_decode_attn_append(const uint16_t *q_in, int q_head_stride, const uint16_t *k_in,
+                           const uint16_t *v_in, const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                           const float *rope_table, int64_t rope_max_pos, const int32_t *positions,
+                           const int64_t *slot_mapping, uint16_t *k_pages, uint16_t *v_pages,
+                           int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
+                           const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
+                           float scale, uint16_t *out, void *workspace, size_t workspace_bytes,
+                           void *stream) {
+    int st = decode_checks(q_in, k_pages, v_pages, num_pages, block_tables, max_pages_per_seq,
+                           seq_lens, batch, num_queries, max_seq_len, workspace, workspace_bytes);
+    if (st != PGC_OK) return st;
+    if (!out || !std::isfinite(scale) || !k_in || !v_in || !rope_table || !positions || !slot_mapping ||
+        rope_max_pos <= 0)
+        return PGC_ERR_INVALID;
+    if (q_head_stride != PGC_HEAD_DIM && q_head_stride != 2 * PGC_HEAD_DIM) return PGC_ERR_INVALID;
+    CUtensorMap tk, tv;
+    if ((st = pool_tensor_map(k_pages, num_pages, &tk)) != PGC_OK) return st;
+    if ((st = pool_tensor_map(v_pages, num_pages, &tv)) != PGC_OK) return st;
+    DecodeAppend app;
+    app.q_in = q_in;
+    app.q_head_stride = q_head_stride;
+    app.k_in = k_in;
+    app.v_in = v_in;
+    app.q_norm_w = q_norm_w;
+    app.k_norm_w = k_norm_w;
+    app.rope = rope_table;
+    app.rope_max_pos = rope_max_pos;
+    app.positions = positions;
+    app.slots = slot_mapping;
+    app.k_pages = k_pages;
+    app.v_pages = v_pages;
+    app.num_pages = num_pages;
+    // packed q | gate rows: the gate is the second half of each 512-wide head row
+    const uint16_t *gate = q_head_stride == 2 * PGC_HEAD_DIM ? q_in + PGC_HEAD_DIM : nullptr;
+    return cuda_status(launch_decode(nullptr, tk, tv, num_pages, block_tables, max_pages_per_seq, seq_lens,
+                                     batch, num_queries, max_seq_len, scale, gate, out, nullptr, workspace,
+                                     current_sm_count(), static_cast<cudaStream_t>(stream), &app,
+                                     q_head_stride));
+}
+
 int pgc_decode_attn_static(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
                            int64_t num_pages, const int32_t *block_tables,
                            int max_pages_per_seq, const int32_t *seq_lens, int batch,

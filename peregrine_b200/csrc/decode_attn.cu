@@ -44,7 +44,8 @@ constexpr int kMinPagesPerSplit = 4;
 constexpr int kMaxPagesPerSplit = 64;
 
 struct SplitParams {
-    const uint16_t *q;
+    const uint16_t *q;           // rotated query rows, or nullptr with `app` set
+    DecodeAppend app;            // fused decode append (app.q_in != nullptr)
     const int32_t *block_tables;
     const int32_t *seq_lens;
     float *ws;  // [rows][max_splits][258], row = (seq * nq + j) * 16 + head
@@ -61,11 +62,15 @@ struct SmemLayout {
     static constexpr int kQOff = kStageOff + kStages * kStageBytes;
     static constexpr int kMOff = kQOff + 16 * kQRowBytes;
     static constexpr int kLOff = kMOff + kConsumers * 16 * 4;
-    static constexpr int kBarOff = kLOff + kConsumers * 16 * 4;
+    static constexpr int kTabOff = kLOff + kConsumers * 16 * 4;      // physical page per local page
+    static constexpr int kNewOff = kTabOff + kMaxPagesPerSplit * 4;  // fused append: new K, V rows
+    static constexpr int kNewPageOff = kNewOff + 2 * PGC_MAX_QUERIES * kHeadDim * 2;
+    static constexpr int kBarOff = kNewPageOff + 2 * PGC_MAX_QUERIES * 4;
     static constexpr int kBytes = kBarOff + 2 * kStages * 8;
 };
 constexpr int kSmemBytes = SmemLayout::kBytes + 1024;  // + alignment slack
 
+template <bool kFused>
 __global__ void __launch_bounds__(kThreads, 2)
     decode_split_kernel(const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, const SplitParams p) {
@@ -125,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     page = 0;
                 }
                 uint8_t *stage = smem + SmemLayout::kStageOff + s * kStageBytes;
+                if (kFused) reinterpret_cast<int32_t *>(smem + SmemLayout::kTabOff)[i] = page;  // released below
                 mbar_arrive_expect_tx(&full[s], kStageBytes);
                 const int row = (page * kNumKvHeads + kvh) * kPage;
 #pragma unroll
@@ -138,18 +144,112 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---------------------------------------------------------------- consumers
-    // Query rows (loaded while the first K/V pages are in flight): r = j * 4 + g (query token j, head kvh * 4 + g); rows >= nrows are zero.
-    for (int i = threadIdx.x; i < 16 * (kHeadDim / 8); i += kConsumers * 32) {
-        const int r = i / (kHeadDim / 8);
-        const int c = i % (kHeadDim / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < nrows) {
-            const int j = r / kGroup, g = r % kGroup;
-            const uint16_t *src =
-                p.q + ((int64_t)(seq * nq + j) * kNumQHeads + kvh * kGroup + g) * kHeadDim;
-            v = reinterpret_cast<const uint4 *>(src)[c];
+    uint16_t *new_k = reinterpret_cast<uint16_t *>(smem + SmemLayout::kNewOff);  // [nq][256]
+    uint16_t *new_v = new_k + PGC_MAX_QUERIES * kHeadDim;
+    int32_t *new_page = reinterpret_cast<int32_t *>(smem + SmemLayout::kNewPageOff);  // [nq]
+    int32_t *new_row = new_page + PGC_MAX_QUERIES;
+    constexpr bool fused = kFused;
+    if (!fused) {
+        // Query rows (loaded while the first K/V pages are in flight): r = j * 4 + g (query
+        // token j, head kvh * 4 + g); rows >= nrows are zero.
+        for (int i = threadIdx.x; i < 16 * (kHeadDim / 8); i += kConsumers * 32) {
+            const int r = i / (kHeadDim / 8);
+            const int c = i % (kHeadDim / 8);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < nrows) {
+                const int j = r / kGroup, g = r % kGroup;
+                const uint16_t *src =
+                    p.q + ((int64_t)(seq * nq + j) * kNumQHeads + kvh * kGroup + g) * kHeadDim;
+                v = reinterpret_cast<const uint4 *>(src)[c];
+            }
+            *reinterpret_cast<uint4 *>(q_s + r * kQRowBytes + c * 16) = v;
         }
-        *reinterpret_cast<uint4 *>(q_s + r * kQRowBytes + c * 16) = v;
+    } else {
+        // Fused decode append, the arithmetic of pgc_append_kv_rope in decode mode: the query
+        // rows (RMSNorm + RoPE) go straight into the tile, and the new K and V rows of this kv
+        // head into a small stash. Split 0 writes those rows into the pool; every CTA patches them into
+        // the page tile that holds their slot (below), so the attention never depends on reading
+        // back its own global write.
+        const DecodeAppend &a = p.app;
+        // warp g: query head kvh * 4 + g of every token j (tile row j * 4 + g); warp j < nq also
+        // the new K and V rows of token j. All loads are issued in two rounds (positions, then
+        // rows, weights and RoPE rows) before any arithmetic.
+        const int g = warp;
+        const int64_t tb = (int64_t)seq * nq;
+        int32_t pos[PGC_MAX_QUERIES];
+#pragma unroll
+        for (int j = 0; j < PGC_MAX_QUERIES; ++j) pos[j] = j < nq ? a.positions[tb + j] : -1;
+        const int64_t slot = warp < nq ? a.slots[tb + warp] : -1;
+        const int32_t kpos = warp < nq ? a.positions[tb + warp] : -1;  // the K/V token's position
+        float xq[PGC_MAX_QUERIES][8], cq[PGC_MAX_QUERIES], sq[PGC_MAX_QUERIES], qwf[8];
+#pragma unroll
+        for (int j = 0; j < PGC_MAX_QUERIES; ++j) {
+            const bool ok = j < nq && pos[j] >= 0 && pos[j] < a.rope_max_pos;
+            const uint16_t *src = a.q_in + ((tb + j) * kNumQHeads + kvh * kGroup + g) * a.q_head_stride;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) xq[j][jj] = ok ? bf16_bits_to_f32(src[lane + 32 * jj]) : 0.f;
+            cq[j] = ok ? a.rope[(int64_t)pos[j] * kRot + lane] : 0.f;
+            sq[j] = ok ? a.rope[(int64_t)pos[j] * kRot + 32 + lane] : 0.f;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) qwf[jj] = a.q_norm_w != nullptr ? bf16_bits_to_f32(a.q_norm_w[lane + 32 * jj]) : 0.f;
+        const bool kv_ok = warp < nq && kpos >= 0 && kpos < a.rope_max_pos && slot >= 0;
+        const bool page_ok = kv_ok && slot / kPage < a.num_pages;
+        float xk[8], kwf[8], ck = 0.f, sk = 0.f;
+        uint16_t vv[8];
+        if (page_ok) {
+            const int64_t t = tb + warp;
+            const uint16_t *ks = a.k_in + (t * kNumKvHeads + kvh) * kHeadDim;
+            const uint16_t *vs = a.v_in + (t * kNumKvHeads + kvh) * kHeadDim;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                xk[jj] = bf16_bits_to_f32(ks[lane + 32 * jj]);
+                kwf[jj] = a.k_norm_w != nullptr ? bf16_bits_to_f32(a.k_norm_w[lane + 32 * jj]) : 0.f;
+                vv[jj] = vs[lane + 32 * jj];
+            }
+            ck = a.rope[(int64_t)kpos * kRot + lane];
+            sk = a.rope[(int64_t)kpos * kRot + 32 + lane];
+        }
+        // query rows
+#pragma unroll
+        for (int j = 0; j < PGC_MAX_QUERIES; ++j) {
+            uint16_t *qrow = reinterpret_cast<uint16_t *>(q_s + (j * kGroup + g) * kQRowBytes);
+            uint16_t o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (j < nq) {
+                if (pos[j] >= 0 && pos[j] < a.rope_max_pos)
+                    append_row_compute(xq[j], a.q_norm_w != nullptr ? qwf : nullptr, cq[j], sq[j], true, o);
+                else if (lane == 0 && kvh == 0 && split == 0 && g == 0)
+                    record_error(&g_decode_err, kErrPosOutOfRange, tb + j);
+            }
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) qrow[lane + 32 * jj] = o[jj];
+        }
+        // the new K and V rows of token `warp`
+        if (warp < nq) {
+            int32_t page = -1;
+            if (kv_ok && !page_ok) {
+                if (lane == 0 && kvh == 0 && split == 0) record_error(&g_decode_err, kErrSlotOutOfRange, slot);
+            } else if (page_ok) {
+                page = (int32_t)(slot / kPage);
+                uint16_t ko[8];
+                append_row_compute(xk, a.k_norm_w != nullptr ? kwf : nullptr, ck, sk, true, ko);
+                const int64_t off = (((int64_t)page * kNumKvHeads + kvh) * kPage + slot % kPage) * kHeadDim;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    const int d = lane + 32 * jj;
+                    new_k[warp * kHeadDim + d] = ko[jj];
+                    new_v[warp * kHeadDim + d] = vv[jj];
+                    if (split == 0) {
+                        a.k_pages[off + d] = ko[jj];
+                        a.v_pages[off + d] = vv[jj];
+                    }
+                }
+            }
+            if (lane == 0) {
+                new_page[warp] = page;
+                new_row[warp] = (int32_t)(slot % kPage);
+            }
+        }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
 
@@ -186,6 +286,22 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t v_base = smem_u32(vt);
         const int tok0 = tok_begin + i * kPage;
         const int nvalid = min(kPage, tok_end - tok0);
+        if constexpr (fused) {
+            // the new rows of this page (fused append): lane l writes dims 8l..8l+7 of K and V
+            const int32_t phys = reinterpret_cast<const int32_t *>(smem + SmemLayout::kTabOff)[i];
+            bool patched = false;
+            for (int jj = 0; jj < nq; ++jj) {
+                if (new_page[jj] != phys) continue;
+                const int row = new_row[jj];
+                *reinterpret_cast<uint4 *>(kt + swz_page_offset(row, 8 * lane)) =
+                    *reinterpret_cast<const uint4 *>(new_k + jj * kHeadDim + 8 * lane);
+                *reinterpret_cast<uint4 *>(vt + swz_page_offset(row, 8 * lane)) =
+                    *reinterpret_cast<const uint4 *>(new_v + jj * kHeadDim + 8 * lane);
+                patched = true;
+            }
+            if (patched) fence_proxy_async_smem();  // generic writes before any later async refill
+            __syncwarp();
+        }
 
         // S[16 rows x 16 tokens] = Q K^T
         float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -348,6 +464,7 @@ struct MergeParams {
     int rows_per_seq;
     int tokens_per_split;
     const uint16_t *gate;
+    int64_t gate_stride;  // elements between gate rows
     uint16_t *out;      // bf16 output, or
     float *out_partial; // merged (m, l, o) partial
 };
@@ -451,7 +568,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
     }
     float v = (den == 0.f) ? 0.f : acc / den;
     if (p.gate) {
-        const float g = bf16_bits_to_f32(p.gate[row * kHeadDim + d]);
+        const float g = bf16_bits_to_f32(p.gate[row * p.gate_stride + d]);
         v = v * (1.0f / (1.0f + expf(-g)));
     }
     p.out[row * kHeadDim + d] = f32_to_bf16_bits(v);
@@ -538,20 +655,25 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
                           int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
                           const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
                           float scale, const uint16_t *gate, uint16_t *out, float *partials_out,
-                          void *workspace, int sm_count, cudaStream_t stream) {
+                          void *workspace, int sm_count, cudaStream_t stream,
+                          const DecodeAppend *app, int64_t gate_stride) {
     static bool attr_set[64] = {};  // the attribute is per device context
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_split_kernel,
+        cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<false>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_split_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemBytes);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const DecodePlan plan = decode_plan(batch, max_seq_len, sm_count);
     SplitParams sp;
     sp.q = q;
+    if (app != nullptr) sp.app = *app;
     sp.block_tables = block_tables;
     sp.seq_lens = seq_lens;
     sp.ws = static_cast<float *>(workspace);
@@ -562,7 +684,9 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
     sp.max_splits = plan.max_splits;
     sp.scale_log2 = scale * kLog2e;
     dim3 grid(plan.max_splits, kNumKvHeads, batch);
-    cudaError_t le = launch_pdl(decode_split_kernel, grid, dim3(kThreads), kSmemBytes, stream, tk, tv, sp);
+    cudaError_t le = app != nullptr
+                         ? launch_pdl(decode_split_kernel<true>, grid, dim3(kThreads), kSmemBytes, stream, tk, tv, sp)
+                         : launch_pdl(decode_split_kernel<false>, grid, dim3(kThreads), kSmemBytes, stream, tk, tv, sp);
     if (le != cudaSuccess) return le;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -577,6 +701,7 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
     mp.rows_per_seq = num_queries * kNumQHeads;
     mp.tokens_per_split = plan.pages_per_split * kPage;
     mp.gate = gate;
+    mp.gate_stride = gate_stride;
     mp.out = out;
     mp.out_partial = partials_out;
     const int64_t rows = (int64_t)batch * num_queries * kNumQHeads;
@@ -597,6 +722,7 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
     mp.rows_per_seq = 1;
     mp.tokens_per_split = 1;
     mp.gate = gate;
+    mp.gate_stride = kHeadDim;
     mp.out = out;
     mp.out_partial = nullptr;
     if (num_parts <= kMergeRowsMaxParts && part_stride % 2 == 0 &&
@@ -765,7 +891,7 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kSmemBytes);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
@@ -782,7 +908,7 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
     sp.pages_per_split = plan.pages_per_split;
     sp.max_splits = plan.max_splits;
     sp.scale_log2 = scale * kLog2e;
-    cudaError_t e = launch_pdl(decode_split_kernel, dim3(plan.max_splits, kNumKvHeads, 1), dim3(kThreads),
+    cudaError_t e = launch_pdl(decode_split_kernel<false>, dim3(plan.max_splits, kNumKvHeads, 1), dim3(kThreads),
                                kSmemBytes, stream, tk, tv, sp);
     if (e != cudaSuccess) return e;
     CpParams cp;

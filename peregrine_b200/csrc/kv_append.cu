@@ -78,39 +78,10 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
                                : p.k_in + (t * kNumKvHeads + kvh) * kHeadDim;
     const uint16_t *w = is_q ? p.q_norm_w : p.k_norm_w;
 
-    float y[8];
+    uint16_t o[8];
+    append_row_warp(src, w, p.rope + (int64_t)pos * kRot, p.mode == PGC_APPEND_DECODE, lane, o);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) y[j] = bf16_bits_to_f32(src[lane + 32 * j]);
-
-    if (w != nullptr) {
-        float e[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) e[j] = __fmul_rn(y[j], y[j]);
-        const float a0 = __fadd_rn(e[0], e[4]), a1 = __fadd_rn(e[1], e[5]);
-        const float a2 = __fadd_rn(e[2], e[6]), a3 = __fadd_rn(e[3], e[7]);
-        float ss = __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
-#pragma unroll
-        for (int s = 16; s > 0; s >>= 1) ss = __fadd_rn(ss, __shfl_down_sync(0xffffffffu, ss, s));
-        ss = __shfl_sync(0xffffffffu, ss, 0);
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 256.0f), 1e-6f)));
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            y[j] = __fmul_rn(__fmul_rn(y[j], inv), bf16_bits_to_f32(w[lane + 32 * j]));
-    }
-
-    float x1 = y[0], x2 = y[1];  // dims lane and lane + 32: one RoPE pair
-    if (p.mode == PGC_APPEND_DECODE) {
-        x1 = bf16_bits_to_f32(f32_to_bf16_bits(x1));
-        x2 = bf16_bits_to_f32(f32_to_bf16_bits(x2));
-    }
-    const float c = p.rope[(int64_t)pos * kRot + lane];
-    const float s = p.rope[(int64_t)pos * kRot + 32 + lane];
-    const float r1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-    const float r2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
-    dst[lane] = f32_to_bf16_bits(r1);
-    dst[lane + 32] = f32_to_bf16_bits(r2);
-#pragma unroll
-    for (int j = 2; j < 8; ++j) dst[lane + 32 * j] = f32_to_bf16_bits(y[j]);
+    for (int j = 0; j < 8; ++j) dst[lane + 32 * j] = o[j];
 
     if (is_q) {
         if (p.gate_out != nullptr) {

@@ -229,6 +229,54 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+// One appended row (a q head or a k head, 256 dims) held by a warp, lane l owning dims l + 32 j:
+// optional RMSNorm x * (1 / sqrt(mean(x^2) + 1e-6)) * w with the sum in a fixed order, then RoPE
+// on the pairs (l, l + 32) of dims [0, 64) with the host's cos/sin row; in decode mode the pair is
+// rounded to bf16 first (attention.metal:377,389-396). out[j] is dim l + 32 j as bf16. Every
+// step is an explicitly rounded fp32 operation, so the append kernel and the fused decode
+// produce the same bits. append_row_compute takes the row already loaded (x and w as floats).
+__device__ __forceinline__ void append_row_compute(const float (&x)[8], const float *w, float c, float s,
+                                                   bool decode_mode, uint16_t (&out)[8]) {
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = x[j];
+    if (w != nullptr) {
+        float e[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e[j] = __fmul_rn(y[j], y[j]);
+        const float a0 = __fadd_rn(e[0], e[4]), a1 = __fadd_rn(e[1], e[5]);
+        const float a2 = __fadd_rn(e[2], e[6]), a3 = __fadd_rn(e[3], e[7]);
+        float ss = __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_down_sync(0xffffffffu, ss, o));
+        ss = __shfl_sync(0xffffffffu, ss, 0);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 256.0f), 1e-6f)));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(__fmul_rn(y[j], inv), w[j]);
+    }
+    float x1 = y[0], x2 = y[1];  // dims lane and lane + 32: one RoPE pair
+    if (decode_mode) {
+        x1 = bf16_bits_to_f32(f32_to_bf16_bits(x1));
+        x2 = bf16_bits_to_f32(f32_to_bf16_bits(x2));
+    }
+    out[0] = f32_to_bf16_bits(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
+    out[1] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
+#pragma unroll
+    for (int j = 2; j < 8; ++j) out[j] = f32_to_bf16_bits(y[j]);
+}
+
+// The same row with its loads: src and w rows of 256 bf16, rope_row the position's cos | sin.
+__device__ __forceinline__ void append_row_warp(const uint16_t *src, const uint16_t *w, const float *rope_row,
+                                                bool decode_mode, int lane, uint16_t (&out)[8]) {
+    float x[8], wf[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        x[j] = bf16_bits_to_f32(src[lane + 32 * j]);
+        wf[j] = w != nullptr ? bf16_bits_to_f32(w[lane + 32 * j]) : 0.f;
+    }
+    append_row_compute(x, w != nullptr ? wf : nullptr, rope_row[lane], rope_row[32 + lane], decode_mode, out);
+}
+
 // Byte offset of element (row, dim) inside a [4 boxes][16 rows][128 B] page tile written by
 // TMA with 128-byte swizzling: 16-byte unit index XOR (row mod 8).
 __device__ __forceinline__ uint32_t swz_page_offset(int row, int dim) {

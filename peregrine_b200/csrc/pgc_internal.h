@@ -34,11 +34,26 @@ struct DecodePlan {
 };
 DecodePlan decode_plan(int batch, int max_seq_len, int sm_count);
 size_t decode_workspace_bytes(int batch, int num_queries, int max_seq_len, int sm_count);
+// The decode append fused into the split kernel (pgc_decode_attn_append): the inputs of
+// pgc_append_kv_rope in decode mode, token t = seq * num_queries + j.
+struct DecodeAppend {
+    const uint16_t *q_in = nullptr;  // [tokens][16][q_head_stride] bf16 (q, or q | gate)
+    int q_head_stride = 0;
+    const uint16_t *k_in = nullptr, *v_in = nullptr;  // [tokens][4][256]
+    const uint16_t *q_norm_w = nullptr, *k_norm_w = nullptr;
+    const float *rope = nullptr;  // [rope_max_pos][64] cos | sin
+    int64_t rope_max_pos = 0;
+    const int32_t *positions = nullptr;
+    const int64_t *slots = nullptr;
+    uint16_t *k_pages = nullptr, *v_pages = nullptr;
+    int64_t num_pages = 0;
+};
 cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
                           int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
                           const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
                           float scale, const uint16_t *gate, uint16_t *out, float *partials_out,
-                          void *workspace, int sm_count, cudaStream_t stream);
+                          void *workspace, int sm_count, cudaStream_t stream,
+                          const DecodeAppend *app = nullptr, int64_t gate_stride = 256);
 cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_parts,
                                   int64_t part_stride, const uint16_t *gate, uint16_t *out,
                                   cudaStream_t stream);
