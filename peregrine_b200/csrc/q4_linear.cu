@@ -68,12 +68,6 @@ __global__ void __launch_bounds__(256) q4_dequant_kernel(const uint32_t *w, cons
     }
 }
 
-// Two nibbles of a packed word (k = 2j, 2j + 1) as a bf16 pair 128 + q: 0x4300 is 128.0 in
-// bf16 and its last mantissa bit is worth 1, so OR-ing q in gives 128 + q exactly.
-__device__ __forceinline__ uint32_t nib2_bf16(uint32_t word, int j) {
-    const uint32_t t = word >> (8 * j);
-    return ((t & 0xFu) | ((t & 0xF0u) << 12)) | 0x43004300u;
-}
 
 // Decode projection for 1-2 tokens (the reference's single-sequence GEMV,
 // linear_q4_affine_group64_qmv_fast_bf16, linear.metal:64-123) on the CUDA cores: at this batch
@@ -202,6 +196,19 @@ __global__ void __launch_bounds__(256) q4_gemv_kernel(const uint16_t *x, const u
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
             if (lane == 0) y[(int64_t)t * out_dim + r0 + r] = f32_to_bf16_bits(v);
         }
+}
+
+// The four bf16 pairs (128 + q_{2j}, 128 + q_{2j+1}) of a packed word, j = 0..3: the even and
+// odd nibbles are split into bytes once, then one byte permute per pair places them in bytes 0
+// and 2 (selector nibble 8 = the sign of byte 0 of `lo`, which is 0) and one OR adds 0x4300.
+__device__ __forceinline__ void nib_pairs_bf16(uint32_t word, uint32_t (&pr)[4]) {
+    const uint32_t lo = word & 0x0F0F0F0Fu, hi = (word >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t r;
+        asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(lo), "r"(hi), "r"(0x8480u | (4u + j) << 8 | j));
+        pr[j] = r | 0x43004300u;
+    }
 }
 
 // ------------------------------------------------------------------ tcgen05 pieces (cta_group::1)
@@ -527,8 +534,9 @@ __global__ void __launch_bounds__(20 * 32, 1)
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
                     const int u = 4 * hh + jj;
-                    *reinterpret_cast<uint4 *>(bf + ((u ^ (row & 7)) << 4)) =
-                        make_uint4(nib2_bf16(wv[jj], 0), nib2_bf16(wv[jj], 1), nib2_bf16(wv[jj], 2), nib2_bf16(wv[jj], 3));
+                    uint32_t pr[4];
+                    nib_pairs_bf16(wv[jj], pr);
+                    *reinterpret_cast<uint4 *>(bf + ((u ^ (row & 7)) << 4)) = make_uint4(pr[0], pr[1], pr[2], pr[3]);
                 }
             }
             fence_proxy_async_smem();  // the bf16 tiles are read by the tensor cores
