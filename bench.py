@@ -50,9 +50,9 @@ def parse():
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1-3 side figures")
     ap.add_argument("--only-configs", action="store_true",
                     help="time only the config 1-3 side figures (profiling aid)")
-    ap.add_argument("--profile-kernels", choices=["q4", "linear"], default=None,
-                    help="small case of the q4 decode projection or the gated-delta prefill, 3 "
-                         "launches each, for ncu captures")
+    ap.add_argument("--profile-kernels", choices=["q4", "linear", "restore", "verify"], default=None,
+                    help="small cases for ncu captures: the q4 decode projection, the gated-delta "
+                         "prefill, the config-2 restore, one config-3 verify layer (fused and two-call)")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="profiling aid: config 2's causal prefill on one layer, 3 launches")
     return ap.parse_args()
@@ -913,7 +913,7 @@ def profile_prefill():
 
 
 def profile_kernels(which):
-    """Small cases for ncu captures of the next-row kernels, 3 launches each.
+    """Small cases for ncu captures (3 launches each unless stated).
     q4: the 4096 -> 8192 q|gate projection of 64 decode tokens (q4_tc_kernel; 18 MB of packed
     weights, scales and biases; four weight copies so that launches read from HBM).
     linear: one gated-delta prefill layer over a 1600-token chunk (gated_delta_prep_kernel,
@@ -933,7 +933,7 @@ def profile_kernels(which):
         y = torch.empty((T, o), dtype=bf, device="cuda")
         for k in range(3):
             capi.q4_linear(x, ws[k], sc, bi, y)
-    else:
+    elif which == "linear":
         T, C, HV = 1600, capi.LIN_CONV_DIM, capi.LIN_VALUE_HEADS
         xs = torch.randn((T, C), dtype=bf, device="cuda", generator=g)
         at = torch.randn((T, HV), dtype=bf, device="cuda", generator=g)
@@ -945,8 +945,57 @@ def profile_kernels(which):
         ws = torch.empty(capi.gated_delta_prefill_workspace_bytes(T), dtype=torch.uint8, device="cuda")
         for _ in range(3):
             capi.gated_delta_prefill(rec, True, xs, at, bt, a_log, dtb, yt, ws)
+    elif which == "restore":
+        # config 2's restore, once: 8 layers of dense K/V into permuted pages, the hidden rows and
+        # the 48 linear states (about 1.1 GB each way on the device)
+        P, layers = 24576, LAYERS
+        pages = (P + 1600 + PAGE - 1) // PAGE
+        stride = capi.full_cache_stride_for_max_seq(P)
+        sk = [torch.randn((NKV, stride, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+        sv = [torch.randn((NKV, D, stride), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
+        sh = torch.randn((P, 4096), dtype=bf, device="cuda", generator=g)
+        sgd = [torch.randn(32 * 128 * 128, device="cuda", generator=g) for _ in range(24)]
+        scv = [torch.randn(3 * 8192, dtype=bf, device="cuda", generator=g) for _ in range(24)]
+        kp = [torch.empty((pages, NKV, PAGE, D), dtype=bf, device="cuda") for _ in range(layers)]
+        vp = [torch.empty((pages, NKV, PAGE, D), dtype=bf, device="cuda") for _ in range(layers)]
+        lh = torch.empty((P + 1600, 4096), dtype=bf, device="cuda")
+        live = [torch.empty_like(t) for t in sgd + scv]
+        table = torch.randperm(pages, device="cuda", generator=g).to(torch.int32)
+        regions = [(d, s_, s_.numel() * s_.element_size()) for d, s_ in zip(live, sgd + scv)]
+        for l in range(layers):
+            capi.kv_restore_dense(sk[l], sv[l], stride, 0, kp[l], vp[l], table, 0, P)
+        capi.copy_rows(lh, sh, P, 4096 * 2, 4096 * 2, 4096 * 2)
+        capi.copy_regions(regions)
+    elif which == "verify":
+        # one config-3 layer (2 queries over 32768 cached tokens, RMSNorm weights, packed q | gate):
+        # the fused append + decode, then the two-call form
+        L = 32768
+        pages = (L + 2 + PAGE - 1) // PAGE
+        kp = torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g)
+        vp = torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g)
+        table = torch.randperm(pages, device="cuda", generator=g).to(torch.int32).view(1, -1)
+        q_in = torch.randn((2, NQ, 2 * D), dtype=bf, device="cuda", generator=g)
+        k_in = torch.randn((2, NKV, D), dtype=bf, device="cuda", generator=g)
+        v_in = torch.randn((2, NKV, D), dtype=bf, device="cuda", generator=g)
+        qw = torch.randn(D, dtype=bf, device="cuda", generator=g)
+        kw = torch.randn(D, dtype=bf, device="cuda", generator=g)
+        rope = torch.from_numpy(capi.rope_table(L + 2)).cuda()
+        pos = torch.tensor([L, L + 1], dtype=torch.int32, device="cuda")
+        slots = table[0].long()[pos.long() // PAGE] * PAGE + pos.long() % PAGE
+        seq = torch.tensor([L + 2], dtype=torch.int32, device="cuda")
+        ws = torch.empty(capi.decode_workspace_bytes(1, 2, L + 2), dtype=torch.uint8, device="cuda")
+        q = torch.empty((2, NQ, D), dtype=bf, device="cuda")
+        gate = torch.empty_like(q)
+        out = torch.empty((1, 2, NQ, D), dtype=bf, device="cuda")
+        for _ in range(3):
+            capi.decode_attn_append(q_in, k_in, v_in, rope, pos, slots, kp, vp, table, seq, L + 2, SCALE, out, ws,
+                                    num_queries=2, q_norm_w=qw, k_norm_w=kw)
+        for _ in range(3):
+            capi.append_kv_rope(q_in, q, k_in, v_in, rope, pos, slots, kp, vp, gate_out=gate, q_norm_w=qw,
+                                k_norm_w=kw)
+            capi.decode_attn(q, kp, vp, table, seq, L + 2, SCALE, out, ws, num_queries=2, gate=gate)
     torch.cuda.synchronize()
-    print(json.dumps({"profile": which, "launches": 3}), flush=True)
+    print(json.dumps({"profile": which}), flush=True)
 
 
 def main():
