@@ -62,11 +62,8 @@ struct SmemLayout {
     static constexpr int kQOff = kStageOff + kStages * kStageBytes;
     static constexpr int kMOff = kQOff + 16 * kQRowBytes;
     static constexpr int kLOff = kMOff + kConsumers * 16 * 4;
-    static constexpr int kTabOff = kLOff + kConsumers * 16 * 4;      // physical page per local page
-    static constexpr int kNewOff = kTabOff + kMaxPagesPerSplit * 4;  // fused append: new K, V rows
-    static constexpr int kNewPageOff = kNewOff + 2 * PGC_MAX_QUERIES * kHeadDim * 2;
-    static constexpr int kBarOff = kNewPageOff + 2 * PGC_MAX_QUERIES * 4;
-    static constexpr int kBytes = kBarOff + 2 * kStages * 8;
+    static constexpr int kBarOff = kLOff + kConsumers * 16 * 4;
+    static constexpr int kBytes = kBarOff + (2 * kStages + 1) * 8;  // + kv_ready (fused append)
 };
 constexpr int kSmemBytes = SmemLayout::kBytes + 1024;  // + alignment slack
 
@@ -100,11 +97,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
+    uint64_t *kv_ready = empty + kStages;  // fused append: the new K/V rows are in the pool
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
+        if (kFused) mbar_init(kv_ready, nq);
         fence_mbar_init();
     }
     __syncthreads();  // barriers initialised: the producer may start streaming K/V now
@@ -115,6 +114,12 @@ __global__ void __launch_bounds__(kThreads, 2)
             tma_prefetch_desc(&tmk);
             tma_prefetch_desc(&tmv);
             const uint64_t pol = l2_policy_evict_first();
+            // fused append: the pages holding a new token are loaded only after this CTA has
+            // written the token's K/V rows into the pool (kv_ready), so the tile carries them
+            int32_t newpos[PGC_MAX_QUERIES];
+#pragma unroll
+            for (int j = 0; j < PGC_MAX_QUERIES; ++j)
+                newpos[j] = (kFused && j < nq) ? p.app.positions[(int64_t)seq * nq + j] : -1;
             const int32_t *table =
                 p.block_tables + (int64_t)seq * p.max_pages_per_seq + split * p.pages_per_split;
             for (int i = 0; i < n_pages; ++i) {
@@ -129,8 +134,18 @@ __global__ void __launch_bounds__(kThreads, 2)
                     record_error(&g_decode_err, kErrPageOutOfRange, page);
                     page = 0;
                 }
+                if (kFused) {
+                    const int tok0 = tok_begin + i * kPage;
+                    bool holds_new = false;
+#pragma unroll
+                    for (int j = 0; j < PGC_MAX_QUERIES; ++j)
+                        holds_new |= newpos[j] >= tok0 && newpos[j] < tok0 + kPage && newpos[j] < tok_end;
+                    if (holds_new && !mbar_wait_bounded(kv_ready, 0)) {
+                        record_error(&g_decode_err, kErrWaitTimeout, 3);
+                        return;
+                    }
+                }
                 uint8_t *stage = smem + SmemLayout::kStageOff + s * kStageBytes;
-                if (kFused) reinterpret_cast<int32_t *>(smem + SmemLayout::kTabOff)[i] = page;  // released below
                 mbar_arrive_expect_tx(&full[s], kStageBytes);
                 const int row = (page * kNumKvHeads + kvh) * kPage;
 #pragma unroll
@@ -144,10 +159,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---------------------------------------------------------------- consumers
-    uint16_t *new_k = reinterpret_cast<uint16_t *>(smem + SmemLayout::kNewOff);  // [nq][256]
-    uint16_t *new_v = new_k + PGC_MAX_QUERIES * kHeadDim;
-    int32_t *new_page = reinterpret_cast<int32_t *>(smem + SmemLayout::kNewPageOff);  // [nq]
-    int32_t *new_row = new_page + PGC_MAX_QUERIES;
     constexpr bool fused = kFused;
     if (!fused) {
         // Query rows (loaded while the first K/V pages are in flight): r = j * 4 + g (query
@@ -166,10 +177,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
     } else {
         // Fused decode append, the arithmetic of pgc_append_kv_rope in decode mode: the query
-        // rows (RMSNorm + RoPE) go straight into the tile, and the new K and V rows of this kv
-        // head into a small stash. Split 0 writes those rows into the pool; every CTA patches them into
-        // the page tile that holds their slot (below), so the attention never depends on reading
-        // back its own global write.
+        // rows (RMSNorm + RoPE) go straight into the tile; the new K and V rows of this kv head
+        // are written into the pool by the CTA whose token range holds them, before its producer
+        // loads those pages (kv_ready), so the attention reads them as after a separate append.
         const DecodeAppend &a = p.app;
         // warp g: query head kvh * 4 + g of every token j (tile row j * 4 + g); warp j < nq also
         // the new K and V rows of token j. All loads are issued in two rounds (positions, then
@@ -181,23 +191,35 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int j = 0; j < PGC_MAX_QUERIES; ++j) pos[j] = j < nq ? a.positions[tb + j] : -1;
         const int64_t slot = warp < nq ? a.slots[tb + warp] : -1;
         const int32_t kpos = warp < nq ? a.positions[tb + warp] : -1;  // the K/V token's position
+        // The appended tokens normally sit at L - nq + j: their RoPE rows are fetched for that
+        // guess in the same round as the positions, and fetched again only where a position
+        // differs.
         float xq[PGC_MAX_QUERIES][8], cq[PGC_MAX_QUERIES], sq[PGC_MAX_QUERIES], qwf[8];
 #pragma unroll
         for (int j = 0; j < PGC_MAX_QUERIES; ++j) {
-            const bool ok = j < nq && pos[j] >= 0 && pos[j] < a.rope_max_pos;
+            const int32_t guess = L - nq + j;
+            const bool gok = j < nq && guess >= 0 && guess < a.rope_max_pos;
+            cq[j] = gok ? a.rope[(int64_t)guess * kRot + lane] : 0.f;
+            sq[j] = gok ? a.rope[(int64_t)guess * kRot + 32 + lane] : 0.f;
             const uint16_t *src = a.q_in + ((tb + j) * kNumQHeads + kvh * kGroup + g) * a.q_head_stride;
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) xq[j][jj] = ok ? bf16_bits_to_f32(src[lane + 32 * jj]) : 0.f;
-            cq[j] = ok ? a.rope[(int64_t)pos[j] * kRot + lane] : 0.f;
-            sq[j] = ok ? a.rope[(int64_t)pos[j] * kRot + 32 + lane] : 0.f;
+            for (int jj = 0; jj < 8; ++jj) xq[j][jj] = j < nq ? bf16_bits_to_f32(src[lane + 32 * jj]) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < PGC_MAX_QUERIES; ++j) {
+            const bool ok = j < nq && pos[j] >= 0 && pos[j] < a.rope_max_pos;
+            if (ok && pos[j] != L - nq + j) {
+                cq[j] = a.rope[(int64_t)pos[j] * kRot + lane];
+                sq[j] = a.rope[(int64_t)pos[j] * kRot + 32 + lane];
+            }
         }
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) qwf[jj] = a.q_norm_w != nullptr ? bf16_bits_to_f32(a.q_norm_w[lane + 32 * jj]) : 0.f;
-        const bool kv_ok = warp < nq && kpos >= 0 && kpos < a.rope_max_pos && slot >= 0;
-        const bool page_ok = kv_ok && slot / kPage < a.num_pages;
+        // the K/V token's rows and its RoPE row (for the guessed position) in the same round
         float xk[8], kwf[8], ck = 0.f, sk = 0.f;
         uint16_t vv[8];
-        if (page_ok) {
+        const int32_t kguess = L - nq + warp;
+        if (warp < nq) {
             const int64_t t = tb + warp;
             const uint16_t *ks = a.k_in + (t * kNumKvHeads + kvh) * kHeadDim;
             const uint16_t *vs = a.v_in + (t * kNumKvHeads + kvh) * kHeadDim;
@@ -207,6 +229,14 @@ __global__ void __launch_bounds__(kThreads, 2)
                 kwf[jj] = a.k_norm_w != nullptr ? bf16_bits_to_f32(a.k_norm_w[lane + 32 * jj]) : 0.f;
                 vv[jj] = vs[lane + 32 * jj];
             }
+            if (kguess >= 0 && kguess < a.rope_max_pos) {
+                ck = a.rope[(int64_t)kguess * kRot + lane];
+                sk = a.rope[(int64_t)kguess * kRot + 32 + lane];
+            }
+        }
+        const bool kv_ok = warp < nq && kpos >= 0 && kpos < a.rope_max_pos && slot >= 0;
+        const bool page_ok = kv_ok && slot / kPage < a.num_pages;
+        if (page_ok && kpos != kguess) {
             ck = a.rope[(int64_t)kpos * kRot + lane];
             sk = a.rope[(int64_t)kpos * kRot + 32 + lane];
         }
@@ -224,31 +254,25 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int jj = 0; jj < 8; ++jj) qrow[lane + 32 * jj] = o[jj];
         }
-        // the new K and V rows of token `warp`
+        // the new K and V rows of token `warp`, written into the pool by the CTA whose token
+        // range holds its position (split 0 for a position past the sequence); every warp
+        // j < nq then releases kv_ready after a proxy fence, so the producer's TMA loads see them
         if (warp < nq) {
-            int32_t page = -1;
             if (kv_ok && !page_ok) {
                 if (lane == 0 && kvh == 0 && split == 0) record_error(&g_decode_err, kErrSlotOutOfRange, slot);
-            } else if (page_ok) {
-                page = (int32_t)(slot / kPage);
+            } else if (page_ok && ((kpos >= tok_begin && kpos < tok_end) || (split == 0 && kpos >= L))) {
                 uint16_t ko[8];
                 append_row_compute(xk, a.k_norm_w != nullptr ? kwf : nullptr, ck, sk, true, ko);
-                const int64_t off = (((int64_t)page * kNumKvHeads + kvh) * kPage + slot % kPage) * kHeadDim;
+                const int64_t off = (((slot / kPage) * kNumKvHeads + kvh) * kPage + slot % kPage) * kHeadDim;
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) {
-                    const int d = lane + 32 * jj;
-                    new_k[warp * kHeadDim + d] = ko[jj];
-                    new_v[warp * kHeadDim + d] = vv[jj];
-                    if (split == 0) {
-                        a.k_pages[off + d] = ko[jj];
-                        a.v_pages[off + d] = vv[jj];
-                    }
+                    a.k_pages[off + lane + 32 * jj] = ko[jj];
+                    a.v_pages[off + lane + 32 * jj] = vv[jj];
                 }
             }
-            if (lane == 0) {
-                new_page[warp] = page;
-                new_row[warp] = (int32_t)(slot % kPage);
-            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(kv_ready);
         }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
@@ -286,22 +310,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t v_base = smem_u32(vt);
         const int tok0 = tok_begin + i * kPage;
         const int nvalid = min(kPage, tok_end - tok0);
-        if constexpr (fused) {
-            // the new rows of this page (fused append): lane l writes dims 8l..8l+7 of K and V
-            const int32_t phys = reinterpret_cast<const int32_t *>(smem + SmemLayout::kTabOff)[i];
-            bool patched = false;
-            for (int jj = 0; jj < nq; ++jj) {
-                if (new_page[jj] != phys) continue;
-                const int row = new_row[jj];
-                *reinterpret_cast<uint4 *>(kt + swz_page_offset(row, 8 * lane)) =
-                    *reinterpret_cast<const uint4 *>(new_k + jj * kHeadDim + 8 * lane);
-                *reinterpret_cast<uint4 *>(vt + swz_page_offset(row, 8 * lane)) =
-                    *reinterpret_cast<const uint4 *>(new_v + jj * kHeadDim + 8 * lane);
-                patched = true;
-            }
-            if (patched) fence_proxy_async_smem();  // generic writes before any later async refill
-            __syncwarp();
-        }
 
         // S[16 rows x 16 tokens] = Q K^T
         float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
