@@ -310,11 +310,12 @@ __device__ __forceinline__ bool q4_wait(uint64_t *bar, uint32_t parity, volatile
 // group), 17-18 x sums (token halves), 19 TMA producer. The pipeline moves in steps of two
 // groups (a step's waits, proxy fence and commits are paid once per 128 inputs):
 //   - W ring: the packed words of 4 groups (2 steps) per slot ([128 rows][128 B], 128-byte
-//     swizzle, so a request moves 128 contiguous bytes of a row), 3 slots ahead; the converters
+//     swizzle, so a request moves 128 contiguous bytes of a row), 2 slots ahead; the converters
 //     release a slot when they have unpacked its last step;
 //   - X ring: one step's two x tiles (the MMA's B operands, [NP][64] bf16 swizzled, rows past T
 //     read as zero) and their sums per slot; released by the MMA's commit and the epilogue;
-//   - bf16 slots: one step's two weight tiles (the MMA's A operands, [128][64] swizzled);
+//   - bf16 slots: one step's two weight tiles (the MMA's A operands, [128][64] swizzled), 3 or 4
+//     of them, so converting step s does not wait on the MMAs of step s - 2;
 //   - TMEM: two buffers of a step's two partial-sum tiles [128 lanes][NP].
 // Each converter warp unpacks its rows on its own (no barrier across the converters) and issues
 // no copies, so the proxy fence that hands its stores to the tensor cores has nothing in flight
@@ -322,11 +323,11 @@ __device__ __forceinline__ bool q4_wait(uint64_t *bar, uint32_t parity, volatile
 template <int NP>
 struct Q4TcCfg {
     static constexpr int kGW = 4;                       // groups per W slot
-    static constexpr int kNW = 4;                       // W slots
+    static constexpr int kNW = 3;                       // W slots
     static constexpr int kLAW = kNW - 1;                // W slots loaded ahead
     static constexpr int kNX = NP == 64 ? 3 : 4;        // X slots (steps)
     static constexpr int kLAX = kNX - 1;                // steps of x loaded ahead
-    static constexpr int kNB = 2;                       // bf16 slots (steps)
+    static constexpr int kNB = NP == 16 ? 4 : 3;        // bf16 slots (steps)
     static constexpr int kTB = 2;                       // TMEM buffers (steps)
     static constexpr int kXBytes = NP * 128;            // one x tile [NP][64] bf16, swizzled
     static constexpr int kXSum = 2 * kXBytes;           // offset of the x sums [2][NP] in a slot
@@ -336,7 +337,7 @@ struct Q4TcCfg {
     static constexpr int kX = kW + kNW * 16384;         // [kNX] x slots
     static constexpr int kSc = kX + kNX * kXStride;     // scales, then biases
     static constexpr int kTmemCols = kTB * 2 * NP < 32 ? 32 : kTB * 2 * NP;
-    static constexpr int kMaxG = 64;  // groups per CTA slice (scales and biases in shared memory)
+    static constexpr int kMaxG = 32;  // groups per CTA slice (scales and biases in shared memory)
     static constexpr int kThreads = 20 * 32;
     static_assert(NP * 128 * 4 <= kNB * 32768, "split-K tile fits in the bf16 slots");
     // scales/biases: [128][G] u16 rows padded to 16 bytes; barriers after them
