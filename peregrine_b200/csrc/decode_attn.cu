@@ -799,26 +799,81 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
     if (np > p.max_splits) np = p.max_splits;
     const float *base = p.parts + (int64_t)r * p.max_splits * kPartial;
     float ma = -INFINITY;
-    for (int c = tid; c < np; c += 256) ma = fmaxf(ma, base[(int64_t)c * kPartial]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
-    if (lane == 0) wm[warp] = ma;
-    __syncthreads();
-    ma = wm[0];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) ma = fmaxf(ma, wm[w]);
     float den = 0.f, acc = 0.f;
+    constexpr int kCached = 16;  // parts per warp held in registers: rows of up to 128 splits
+    if (np <= 8 * kCached) {
+        // one round of loads: every (m, l, o[d]) of this warp's splits, then the maximum, the
+        // weights and the sums from registers (the order of the sums is the streaming path's)
+        float mc[kCached], lc[kCached], oc[kCached];
+#pragma unroll
+        for (int i = 0; i < kCached; ++i) {
+            const int c = warp + 8 * i;
+            mc[i] = -INFINITY;
+            lc[i] = oc[i] = 0.f;
+            if (c < np) {
+                const float *pc = base + (int64_t)c * kPartial;
+                mc[i] = pc[0];
+                lc[i] = pc[1];
+                oc[i] = pc[2 + d0 + lane];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kCached; ++i) ma = fmaxf(ma, mc[i]);
+        if (lane == 0) wm[warp] = ma;  // m is the same in every lane of the warp
+        __syncthreads();
+        ma = wm[0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) ma = fmaxf(ma, wm[w]);
+#pragma unroll
+        for (int i = 0; i < kCached; ++i) {
+            if (mc[i] != -INFINITY) {
+                const float w = exp2f((mc[i] - ma) * kLog2e);
+                den += lc[i] * w;
+                acc += oc[i] * w;
+            }
+        }
+    } else {
+        for (int c = tid; c < np; c += 256) ma = fmaxf(ma, base[(int64_t)c * kPartial]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+        if (lane == 0) wm[warp] = ma;
+        __syncthreads();
+        ma = wm[0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) ma = fmaxf(ma, wm[w]);
 #pragma unroll 4
-    for (int c = warp; c < np; c += 8) {
-        const float *pc = base + (int64_t)c * kPartial;
-        const float mc = pc[0];
-        const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - ma) * kLog2e);
-        den += pc[1] * w;
-        acc += pc[2 + d0 + lane] * w;
+        for (int c = warp; c < np; c += 8) {
+            const float *pc = base + (int64_t)c * kPartial;
+            const float mc = pc[0];
+            const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - ma) * kLog2e);
+            den += pc[1] * w;
+            acc += pc[2 + d0 + lane] * w;
+        }
     }
     if (lane == 0) wden[warp] = den;
     wacc[warp][lane] = acc;
     __syncthreads();
+    if (p.world == 1) {
+        // nothing to exchange: the rank partial is the result (the same arithmetic as the
+        // one-part merge below: weight exp2(0) = 1)
+        if (warp == 0) {
+            float sacc = 0.f, sden = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                sacc += wacc[w][lane];
+                sden += wden[w];
+            }
+            const int dd = d0 + lane;
+            const float d2 = (ma == -INFINITY) ? 0.f : sden;
+            float v = (d2 == 0.f) ? 0.f : ((ma == -INFINITY) ? 0.f : sacc) / d2;
+            if (p.gate) {
+                const float g = bf16_bits_to_f32(p.gate[r * kHeadDim + dd]);
+                v = v * (1.0f / (1.0f + expf(-g)));
+            }
+            p.out[r * kHeadDim + dd] = f32_to_bf16_bits(v);
+        }
+        return;
+    }
     // this CTA's slice of the rank partial -> every rank's slot [parity][rank][r]
     const int parity = (int)(p.epoch & 1u);
     if (warp < p.world) {
