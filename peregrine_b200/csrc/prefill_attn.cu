@@ -590,17 +590,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
             tmem_wait_ld();
             if (threadIdx.x == 0) PF_TRACE(5, j);
             const int key0 = (tb + j) * kBNp + cg * 32;
-            float mx = -INFINITY;
-            if (key0 + 31 <= vis && row_ok) {
+            if (!(key0 + 31 <= vis && row_ok)) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    sv[i] = (row_ok && key0 + i <= vis) ? sv[i] : -INFINITY;
-                    mx = fmaxf(mx, sv[i]);
-                }
+                for (int i = 0; i < 32; ++i) sv[i] = (row_ok && key0 + i <= vis) ? sv[i] : -INFINITY;
             }
+            // four independent chains of 3-input maxima
+            float mq[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+            for (int i = 4; i < 32; i += 8)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) mq[k] = fmax3(mq[k], sv[i + 2 * k], sv[i + 2 * k + 1]);
+            float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
             red[cg * kBM + r] = mx;
             // all four quarters have read S tile b (so P may overwrite it) and posted their max
             asm volatile("bar.sync %0, 128;" ::"r"(1 + qd) : "memory");
@@ -615,16 +615,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                 m = m_new;
             }
             const float m_use = (m == -INFINITY) ? 0.f : m;
-            float ps = 0.f;
+            // paired fp32 FMAs and adds (sm_100 f32x2): half the issue slots of scalar ones
+            const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
+            float2 ps2 = make_float2(0.f, 0.f);
             uint32_t pw[16];
 #pragma unroll
             for (int i = 0; i < 32; i += 2) {
-                const float a0 = fast_exp2(fmaf(sv[i], c, -m_use));
-                const float a1 = fast_exp2(fmaf(sv[i + 1], c, -m_use));
-                ps += a0 + a1;
-                pw[i >> 1] = pack_bf16x2(a0, a1);
+                const float2 x = __ffma2_rn(make_float2(sv[i], sv[i + 1]), c2, nm2);
+                const float2 a = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+                ps2 = __fadd2_rn(ps2, a);
+                pw[i >> 1] = pack_bf16x2(a.x, a.y);
             }
-            l = l * corr + ps;
+            l = l * corr + (ps2.x + ps2.y);
             if (threadIdx.x == 0) PF_TRACE(7, j);
             if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
                 if (!wait_or_abort(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 7)) {
@@ -639,7 +641,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                     tmem_ld32(tmem + lane_addr + col, o);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= corr;
+                    for (int i = 0; i < 32; i += 2) {
+                        const float2 v = __fmul2_rn(make_float2(o[i], o[i + 1]), make_float2(corr, corr));
+                        o[i] = v.x;
+                        o[i + 1] = v.y;
+                    }
                     tmem_st32(tmem + lane_addr + col, o);
                 }
             }
