@@ -138,7 +138,8 @@ size_t pgc_decode_workspace_bytes(int batch, int num_queries, int max_seq_len);
  *   q            [batch][num_queries][16][256] bf16 (device)
  *   k/v_pages    paged pools of `num_pages` pages (layout in the file header)
  *   block_tables [batch][max_pages_per_seq] int32 page ids (device)
- *   seq_lens     [batch] int32 tokens in cache including the queries (device)
+ *   seq_lens     [batch] int32 tokens in cache including the queries (device); 0 marks an
+ *                empty slot, whose output rows are written as zeros
  *   max_seq_len  host-side upper bound of seq_lens (sizes the split grid)
  *   gate         nullable [batch][num_queries][16][256] bf16
  *   out          [batch][num_queries][16][256] bf16

@@ -57,6 +57,20 @@ def test_ragged_batch(cuda, oracle, nq):
     assert_attn_close(got, ref)
 
 
+@pytest.mark.parametrize("nq", [1, 2])
+def test_empty_sequence_slots_give_zero_rows(cuda, oracle, nq):
+    # a serving batch with padding slots (seq_lens 0): their rows come out as zeros (gate or
+    # not) and the other sequences are unaffected
+    lens = [0, 37, 0, 1500, 0]
+    q, kp, vp, table, seq, g = _case(oracle, lens, nq=nq, seed=21, gate=(nq == 2))
+    got = _run(cuda, q, kp, vp, table, seq, nq, g)
+    live = [b for b, L in enumerate(lens) if L > 0]
+    ref, _ = oracle.decode_paged(q[live], kp, vp, np.ascontiguousarray(table[live]), seq[live], SCALE,
+                                 nq, None if g is None else g[live])
+    assert_attn_close(got[live], ref)
+    assert (got[[b for b, L in enumerate(lens) if L == 0]] == 0).all()
+
+
 def test_long_sequences_many_splits(cuda, oracle):
     lens = [20001, 40000, 1111]
     q, kp, vp, table, seq, _ = _case(oracle, lens, seed=9)
