@@ -808,21 +808,44 @@ def run_ours(args, rank, world, local_rank):
     h2d = sum(t.numel() * 2 for t in q_h + k_h + v_h)
     d2h = sum(t.numel() * 2 for t in out_h)
 
+    # The copies run on their own stream, as a serving loop would issue them: layer l + 1's
+    # inputs upload while layer l decodes, and each output downloads behind its layer. Events
+    # keep a layer's buffers from being overwritten while the previous step still uses them.
+    cs = torch.cuda.Stream()
+    in_ready = [torch.cuda.Event() for _ in range(layers)]
+    used = [torch.cuda.Event() for _ in range(layers)]
+    out_read = [torch.cuda.Event() for _ in range(layers)]
+    for l in range(layers):
+        used[l].record(stream)
+        out_read[l].record(cs)
+
     def e2e_step():
+        with torch.cuda.stream(cs):
+            for l in range(layers):
+                cs.wait_event(used[l])
+                q_in[l].copy_(q_h[l], non_blocking=True)
+                k_in[l].copy_(k_h[l], non_blocking=True)
+                v_in[l].copy_(v_h[l], non_blocking=True)
+                in_ready[l].record(cs)
         for l in range(layers):
-            q_in[l].copy_(q_h[l], non_blocking=True)
-            k_in[l].copy_(k_h[l], non_blocking=True)
-            v_in[l].copy_(v_h[l], non_blocking=True)
+            stream.wait_event(in_ready[l])
+            stream.wait_event(out_read[l])
             layer(l)
-            out_h[l].copy_(out[l], non_blocking=True)
+            used[l].record(stream)
+            with torch.cuda.stream(cs):
+                cs.wait_event(used[l])
+                out_h[l].copy_(out[l], non_blocking=True)
+                out_read[l].record(cs)
 
     for _ in range(args.warmup):
         e2e_step()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    cs.wait_stream(stream)
     for _ in range(args.steps):
         e2e_step()
+    stream.wait_stream(cs)  # the last step's downloads are inside the region
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1)
