@@ -131,7 +131,9 @@ def main(ref: Path) -> dict:
 
 
 if __name__ == "__main__":
-    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py <path to the peregrine source tree>")
+    ref = Path(sys.argv[1])
     out = Path(__file__).resolve().parent / "reference_fixtures.json"
     out.write_text(json.dumps(main(ref), indent=1) + "\n")
     print(out)
