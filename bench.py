@@ -389,15 +389,84 @@ def bench_config2(capi, iters=5):
     pcache.close()
     ppool.close()
     r_ms = _ev_time(restore, iters)
+
+    # The same restore from a prefix store in pinned host memory (a snapshot file read into
+    # host RAM): the kernels read the store over the host link, so its bytes cross it once.
+    def pinned(t):
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t)
+        return h
+
+    hk, hv = [pinned(t) for t in store_k], [pinned(t) for t in store_v]
+    hh = pinned(store_h)
+    hregions = [(d, pinned(s_), nb) for d, (_, s_, nb) in zip(live, regions)]
+
+    def restore_pinned():
+        for l in range(layers):
+            capi.kv_restore_dense(hk[l], hv[l], stride, 0, kp[l], vp[l], table, 0, P, stream=s)
+        capi.copy_rows(live_h, hh, P, 4096 * 2, 4096 * 2, 4096 * 2, stream=s)
+        capi.copy_regions(hregions, stream=s)
+
+    rp_ms = _ev_time(restore_pinned, 3)
+
+    # Staged: the copy engines move each layer's dense K/V from the pinned store into one of two
+    # device staging buffers on a copy stream (cudaMemcpyAsync), and the restore kernel scatters
+    # layer l into pages while layer l + 1 is in flight; hidden rows and states go by DMA
+    # straight to their destinations.
+    cs = torch.cuda.Stream()
+    stage_k = [torch.empty_like(store_k[0]) for _ in range(2)]
+    stage_v = [torch.empty_like(store_v[0]) for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+
+    def restore_staged():
+        cs.wait_stream(s)
+        for l in range(layers):
+            b = l % 2
+            with torch.cuda.stream(cs):
+                if l >= 2:
+                    cs.wait_event(freed[b])
+                stage_k[b].copy_(hk[l], non_blocking=True)
+                stage_v[b].copy_(hv[l], non_blocking=True)
+                copied[b].record(cs)
+            s.wait_event(copied[b])
+            capi.kv_restore_dense(stage_k[b], stage_v[b], stride, 0, kp[l], vp[l], table, 0, P,
+                                  stream=s)
+            freed[b].record(s)
+        with torch.cuda.stream(cs):
+            live_h[:P].copy_(hh, non_blocking=True)
+            for d, h, _ in hregions:
+                d.copy_(h, non_blocking=True)
+        s.wait_stream(cs)
+
+    rs_ms = _ev_time(restore_staged, 3)
+    # the staged path must write what the HBM-store restore writes: zero, stage, compare
+    for t in kp + vp + [live_h] + live:
+        t.zero_()
+    restore_staged()
+    torch.cuda.synchronize()
+    got = [t.clone() for t in (kp[0], vp[0], kp[-1], vp[-1], live_h, live[0], live[-1])]
+    restore()
+    torch.cuda.synchronize()
+    staged_ok = all(torch.equal(a, b) for a, b in zip(got, (kp[0], vp[0], kp[-1], vp[-1], live_h,
+                                                            live[0], live[-1])))
+    del got
+    del hk, hv, hh, hregions, stage_k, stage_v
     a_ms = _ev_time(chunk_append, iters)
     p_ms = _ev_time(prefill, iters)
     restore_bytes = layers * P * KV_BYTES_PER_TOKEN + P * 4096 * 2 + 24 * (32 * 128 * 128 * 4 + 3 * 8192 * 2)
     flops = layers * 4 * NQ * D * (T * P + T * (T + 1) / 2)
     append_bytes = layers * T * (NQ * D * 2 * 2 + NKV * D * 2 * 4)
     return {"workload": "config2: restore 24576-token prefix (8 layers KV + MTP hidden + 24 GD/conv "
-                        "states) from an HBM store, then 1600-token chunk append + causal prefill",
+                        "states) from an HBM store (and, timed apart, from a pinned host store), then 1600-token "
+                        "chunk append + causal prefill",
             "restore_ms": round(r_ms, 3), "restore_bytes": restore_bytes,
             "restore_GB_s_read_plus_write": round(2 * restore_bytes / (r_ms * 1e-3) / 1e9, 1),
+            "restore_pinned_store_ms": round(rp_ms, 3),
+            "restore_pinned_store_GB_s_host_link": round(restore_bytes / (rp_ms * 1e-3) / 1e9, 1),
+            "restore_pinned_store_staged_ms": round(rs_ms, 3),
+            "restore_pinned_store_staged_GB_s_host_link": round(restore_bytes / (rs_ms * 1e-3) / 1e9, 1),
+            "restore_pinned_store_staged_matches": staged_ok,
             "hit_share_ms": round(h_ms, 3), "hit_share_bytes_copied": hit_bytes,
             "append_ms": round(a_ms, 3), "append_GB_s": round(append_bytes / (a_ms * 1e-3) / 1e9, 1),
             "prefill_ms": round(p_ms, 3), "prefill_flop": flops,
