@@ -76,15 +76,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
     pdl_trigger();
-    pdl_wait();
     const int split = blockIdx.x;
     const int kvh = blockIdx.y;
     const int seq = blockIdx.z;
-    const int L = p.seq_lens[seq];
-    const int tok_begin = split * p.pages_per_split * kPage;
-    if (tok_begin >= L) return;  // uniform across the CTA
-    const int tok_end = min(L, tok_begin + p.pages_per_split * kPage);
-    const int n_pages = (tok_end - tok_begin + kPage - 1) / kPage;
     const int nq = p.num_queries;
     const int nrows = nq * kGroup;
 
@@ -97,6 +91,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
+    // Shared-memory barriers and the tensor-map prefetch touch no global memory that an earlier
+    // kernel writes, so they run before the programmatic-launch wait, overlapping its tail.
     uint64_t *kv_ready = empty + kStages;  // fused append: the new K/V rows are in the pool
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -106,13 +102,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (kFused) mbar_init(kv_ready, nq);
         fence_mbar_init();
     }
+    if (threadIdx.x == kConsumers * 32) {
+        tma_prefetch_desc(&tmk);
+        tma_prefetch_desc(&tmv);
+    }
+    pdl_wait();
+    const int L = p.seq_lens[seq];
+    const int tok_begin = split * p.pages_per_split * kPage;
+    if (tok_begin >= L) return;  // uniform across the CTA
+    const int tok_end = min(L, tok_begin + p.pages_per_split * kPage);
+    const int n_pages = (tok_end - tok_begin + kPage - 1) / kPage;
     __syncthreads();  // barriers initialised: the producer may start streaming K/V now
 
     if (warp == kConsumers) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            tma_prefetch_desc(&tmk);
-            tma_prefetch_desc(&tmv);
             const uint64_t pol = l2_policy_evict_first();
             // fused append: the pages holding a new token are loaded only after this CTA has
             // written the token's K/V rows into the pool (kv_ready), so the tile carries them
