@@ -36,6 +36,8 @@ D, NQ, NKV, PAGE = 256, 16, 4, 16
 LAYERS = 8
 SCALE = 1.0 / 16
 KV_BYTES_PER_TOKEN = NKV * D * 2 * 2  # K + V per layer
+# One metric string for both arms (ours and --impl reference), so the two lines compare.
+METRIC = "decode-attn achieved HBM GB/s"
 
 
 def parse():
@@ -48,8 +50,6 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1-3 side figures")
-    ap.add_argument("--only-configs", action="store_true",
-                    help="time only the config 1-3 side figures (profiling aid)")
     ap.add_argument("--profile-kernels", choices=["q4", "linear", "restore", "verify"], default=None,
                     help="small cases for ncu captures: the q4 decode projection, the gated-delta "
                          "prefill, the config-2 restore, one config-3 verify layer (fused and two-call)")
@@ -58,12 +58,33 @@ def parse():
     return ap.parse_args()
 
 
-def workload_lengths(workload: str, rank: int, seed: int):
+def workload_lengths(workload: str, rank: int, seed: int, world: int = 1):
+    """This rank's sequence lengths and the layer count. One seeded draw for the whole job
+    (64 sequences per GPU, L ~ U[1024, 65536]; 512 at 8 GPUs, BASELINE config 5a), split
+    across the ranks balanced by tokens: longest first onto the rank with the fewest tokens
+    among those still below 64 sequences. A rank's lengths keep their draw order, so at one
+    GPU the workload is exactly config 4's draw."""
     import numpy as np
-    rng = np.random.default_rng(seed * 1000003 + rank)
-    if workload == "small":
-        return rng.integers(1024, 8193, 8).astype(np.int64), 2
-    return rng.integers(1024, 65537, 64).astype(np.int64), LAYERS
+    rng = np.random.default_rng(seed * 1000003)
+    per, lo, hi, layers = (8, 1024, 8193, 2) if workload == "small" else (64, 1024, 65537, LAYERS)
+    lens = rng.integers(lo, hi, per * world).astype(np.int64)
+    owner = balanced_partition(lens, world, per)
+    return lens[owner == rank], layers
+
+
+def balanced_partition(lens, world: int, per_rank: int):
+    """Owner rank of every sequence: greedy longest-processing-time assignment with a cap of
+    `per_rank` sequences per rank (ties go to the lower rank)."""
+    import numpy as np
+    owner = np.full(len(lens), -1, np.int64)
+    load = [0] * world
+    count = [0] * world
+    for i in sorted(range(len(lens)), key=lambda i: (-int(lens[i]), i)):
+        r = min((r for r in range(world) if count[r] < per_rank), key=lambda r: (load[r], r))
+        owner[i] = r
+        load[r] += int(lens[i])
+        count[r] += 1
+    return owner
 
 
 def step_bytes(lens, layers):
@@ -150,73 +171,135 @@ class ClockSampler:
 
 # ------------------------------------------------------------------------------ CPU legs
 
-def cpu_sample(lens, threads: int, max_tokens: int = 24576, min_seconds: float = 0.0):
-    """Times the CPU restatement of the decode path (oracle, test infrastructure) on a bounded
-    sample of the workload: the first sequences of this rank's draw, up to `max_tokens` cached
-    tokens in total, one layer, OpenMP over (sequence, kv head). Returns (GB/s, seconds, desc)."""
-    import numpy as np
-    from oracle import oracle
-    oracle.set_threads(threads)
-    chosen, total = [], 0
-    for L in lens:
-        L = int(min(L, max_tokens - total)) if total + int(L) > max_tokens else int(L)
-        if L <= 0:
-            break
-        chosen.append(L + 1)
-        total += L + 1
-    pages = [(L + PAGE - 1) // PAGE for L in chosen]
-    npages = sum(pages)
-    kp = oracle.normal_bf16(npages * NKV * PAGE * D, 11).reshape(npages, NKV, PAGE, D)
-    vp = oracle.normal_bf16(npages * NKV * PAGE * D, 12).reshape(npages, NKV, PAGE, D)
-    table = np.zeros((len(chosen), max(pages)), np.int32)
-    o = 0
-    for b, p in enumerate(pages):
-        table[b, :p] = np.arange(o, o + p)
-        o += p
-    q = oracle.normal_bf16(len(chosen) * NQ * D, 13).reshape(len(chosen), 1, NQ, D)
-    seq = np.array(chosen, np.int32)
-    reps = 0
-    t0 = time.perf_counter()
-    while True:  # layer repeats until the sample is long enough (at most the 8 layers)
-        oracle.decode_paged(q, kp, vp, table, seq, SCALE)
-        reps += 1
-        if time.perf_counter() - t0 >= min_seconds or reps >= LAYERS:
-            break
-    dt = time.perf_counter() - t0
-    nbytes = reps * sum(chosen) * KV_BYTES_PER_TOKEN
-    desc = (f"decode attention of {len(chosen)} sequence(s) of the workload draw "
-            f"({sum(chosen)} cached tokens) x {reps} layer(s), oracle C port, {threads} thread(s)")
-    return nbytes / dt / 1e9, dt, desc
+class CpuSample:
+    """The CPU restatement of the decode path (oracle, test infrastructure) over this rank's
+    whole draw: every sequence of the workload, one layer's K/V (random pages, seeded), OpenMP
+    over (sequence, kv head). `run` times decode passes of that layer; the same sample serves
+    the cpu_baseline leg of our arm and every step of the reference arm."""
+
+    def __init__(self, lens, threads: int):
+        import numpy as np
+        from oracle import oracle
+        self.oracle = oracle
+        self.threads = threads
+        oracle.set_threads(threads)
+        self.chosen = [int(L) + 1 for L in lens]  # + the appended row
+        pages = [(L + PAGE - 1) // PAGE for L in self.chosen]
+        npages = sum(pages)
+        self.kp = oracle.normal_bf16(npages * NKV * PAGE * D, 11).reshape(npages, NKV, PAGE, D)
+        self.vp = oracle.normal_bf16(npages * NKV * PAGE * D, 12).reshape(npages, NKV, PAGE, D)
+        self.table = np.zeros((len(self.chosen), max(pages)), np.int32)
+        o = 0
+        for b, p in enumerate(pages):
+            self.table[b, :p] = np.arange(o, o + p)
+            o += p
+        self.q = oracle.normal_bf16(len(self.chosen) * NQ * D, 13).reshape(len(self.chosen), 1, NQ, D)
+        self.seq = np.array(self.chosen, np.int32)
+        self.tokens = sum(self.chosen)
+
+    def run(self, min_seconds: float = 0.0, max_layers: int = 1):
+        """Decode passes until `min_seconds` have elapsed or `max_layers` passes ran.
+        Returns (GB/s of K+V, seconds, passes)."""
+        reps = 0
+        t0 = time.perf_counter()
+        while True:
+            self.oracle.decode_paged(self.q, self.kp, self.vp, self.table, self.seq, SCALE)
+            reps += 1
+            if time.perf_counter() - t0 >= min_seconds or reps >= max_layers:
+                break
+        dt = time.perf_counter() - t0
+        return reps * self.tokens * KV_BYTES_PER_TOKEN / dt / 1e9, dt, reps
+
+    def desc(self, reps: int) -> str:
+        return (f"decode attention of all {len(self.chosen)} sequences of rank 0's workload draw "
+                f"({self.tokens} cached tokens) x {reps} layer pass(es), oracle C port, "
+                f"{self.threads} thread(s)")
 
 
 def run_reference(args, rank, world):
-    """The reference arm: the CPU restatement of the path timed on the host cores."""
+    """The reference arm: the CPU restatement of the path timed on the host cores, on rank 0's
+    sequences of the same draw our arm decodes (one layer of all of them per step)."""
     if rank != 0:
         return
-    lens, layers = workload_lengths(args.workload, 0, args.seed)
+    lens, layers = workload_lengths(args.workload, 0, args.seed, world)
     threads = os.cpu_count() or 1
+    sample = CpuSample(lens, threads)
     vals = []
     for i in range(args.warmup + args.steps):
-        gbs, dt, desc = cpu_sample(lens, threads, max_tokens=65536)
+        gbs, dt, _ = sample.run()
         if i >= args.warmup:
             vals.append((gbs, dt))
     gbs = statistics.median(v[0] for v in vals)
     ms = statistics.median(v[1] for v in vals) * 1e3
     line = {
-        "impl": "reference", "metric": "decode-attn achieved HBM GB/s", "value": round(gbs, 3),
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3),
         "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16 in, fp32 accumulate", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: batched paged decode sample on host cores",
+        "config": {"workload": f"{args.workload}: batched paged decode of rank 0's {len(lens)} "
+                               "sequences on host cores, one layer per step",
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": desc},
+                         "sample": sample.desc(1) + " per step"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "note": "the reference (Zig + Metal) cannot be built or run on Linux; this arm times its "
                 "CPU restatement (oracle/pgo_oracle.c) of the same decode semantics",
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------ output checks
+# The timed configurations are checked in the same run, after their timed regions: the CPU
+# oracle (test infrastructure, fp32 accumulate) is the checker, never the thing measured.
+
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def _u16(t):
+    """bf16 (or int16) device tensor -> host uint16 bits."""
+    import numpy as np
+    import torch
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def _bf(a):
+    import numpy as np
+    return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+def _close(got_u16, ref_f32):
+    import numpy as np
+    g = _bf(got_u16)
+    err = np.abs(g - ref_f32)
+    bad = int(((err > ATOL + RTOL * np.abs(ref_f32)) | ~np.isfinite(g)).sum())
+    return float(err.max()) if err.size else 0.0, bad
+
+
+def check_decode_against_oracle(capi, seqs, q, gate, out, kpool, vpool, table, seq_lens, nq=1):
+    """Decode output of sequences `seqs` (indices into the batch) against the oracle: their
+    pages are copied out of the pools into compact host pools in block-table order."""
+    import numpy as np
+    import torch
+    from oracle import oracle
+    oracle.set_threads(os.cpu_count() or 1)
+    worst, bad = 0.0, 0
+    for b in seqs:
+        L = int(seq_lens[b].item())
+        npg = (L + PAGE - 1) // PAGE
+        idx = table[b, :npg].long()
+        kp = _u16(kpool.index_select(0, idx))
+        vp = _u16(vpool.index_select(0, idx))
+        tb = np.arange(npg, dtype=np.int32).reshape(1, -1)
+        qb = _u16(q[b * nq:(b + 1) * nq]).reshape(1, nq, NQ, D)
+        gb = None if gate is None else _u16(gate[b * nq:(b + 1) * nq]).reshape(1, nq, NQ, D)
+        ref, _ = oracle.decode_paged(qb, kp, vp, tb, np.array([L], np.int32), SCALE, num_queries=nq,
+                                     gate=gb)
+        e, n = _close(_u16(out.reshape(-1, nq, NQ, D)[b]).reshape(1, nq, NQ, D), ref)
+        worst, bad = max(worst, e), bad + n
+        del kp, vp
+    torch.cuda.synchronize()
+    return {"max_abs_err": worst, "bad": bad}
 
 
 # ------------------------------------------------------------------------------ other configs
@@ -292,6 +375,16 @@ def bench_config1(capi, iters=20):
 
     direct, graph_ms = timed(fused_step)
     direct2, graph2 = timed(two_call_step)
+    # output check: the fused launch against the two calls (bit for bit), and against the oracle
+    fused_step(s, 0)
+    out_f = out.clone()
+    two_call_step(s, 0)
+    torch.cuda.synchronize()
+    parity = check_decode_against_oracle(capi, [0], q, None, out, kps[0], vps[0], table, seq)
+    parity.update(fused_equals_two_calls=bool(torch.equal(out_f, out)),
+                  check="fused append+decode vs append then decode (bit-exact); decode vs the "
+                        "CPU oracle (abs 2e-2 + rel 1e-2)")
+    parity["ok"] = parity["bad"] == 0 and parity["fused_equals_two_calls"]
     nbytes = (L + 1) * KV_BYTES_PER_TOKEN + 3 * NQ * D * 2 + 2 * NKV * D * 2
     best = direct if graph_ms is None else min(direct, graph_ms)
     return {"workload": "config1: 1 layer, 4097-token decode + 1 append at pos 4096, fused in one "
@@ -301,13 +394,16 @@ def bench_config1(capi, iters=20):
             "us_per_step_graph": None if graph_ms is None else round(graph_ms * 1e3, 2),
             "us_per_step_two_calls": round(direct2 * 1e3, 2),
             "us_per_step_graph_two_calls": None if graph2 is None else round(graph2 * 1e3, 2),
-            "GB_s": round(nbytes / (best * 1e-3) / 1e9, 1), "algorithmic_bytes": nbytes}
+            "GB_s": round(nbytes / (best * 1e-3) / 1e9, 1), "algorithmic_bytes": nbytes,
+            "parity": parity}
 
 
 def bench_config2(capi, iters=5):
     """Config 2: restore of a 24576-token prefix from an HBM prefix store (8 layers of
     dense-layout K/V into 16-token pages under a random permutation, MTP hidden rows
-    [24576x4096] bf16, 24 gated-delta fp32 states [32x128x128], 24 conv bf16 states [3x8192]),
+    [24576x4096] bf16, 24 gated-delta fp32 states [32x128x128], 24 conv fp32 states [3x8192], the
+    reference's conv state type (state.zig, prefix_persist.zig); BASELINE's text says bf16, the
+    copy is byte-agnostic),
     then a 1600-token chunk: K/V append with RMSNorm + RoPE, causal attention over
     prefix + chunk. The q4 projections are out of scope: the chunk's N(0,1) hidden rows
     [1600x4096] serve directly as Q."""
@@ -324,7 +420,7 @@ def bench_config2(capi, iters=5):
     store_v = [torch.randn((NKV, D, stride), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
     store_h = torch.randn((P, 4096), dtype=bf, device="cuda", generator=g)
     store_gd = [torch.randn(32 * 128 * 128, device="cuda", generator=g) for _ in range(24)]
-    store_cv = [torch.randn(3 * 8192, dtype=bf, device="cuda", generator=g) for _ in range(24)]
+    store_cv = [torch.randn(3 * 8192, device="cuda", generator=g) for _ in range(24)]
     kp = [torch.empty((pages, NKV, PAGE, D), dtype=bf, device="cuda") for _ in range(layers)]
     vp = [torch.empty((pages, NKV, PAGE, D), dtype=bf, device="cuda") for _ in range(layers)]
     live_h = torch.empty((n, 4096), dtype=bf, device="cuda")
@@ -385,7 +481,7 @@ def bench_config2(capi, iters=5):
         ppool.release(t)
 
     h_ms = _ev_time(hit_share, iters)
-    hit_bytes = 24 * (32 * 128 * 128 * 4 + 3 * 8192 * 2)
+    hit_bytes = 24 * (32 * 128 * 128 * 4 + 3 * 8192 * 4)
     pcache.close()
     ppool.close()
     r_ms = _ev_time(restore, iters)
@@ -454,7 +550,7 @@ def bench_config2(capi, iters=5):
     del hk, hv, hh, hregions, stage_k, stage_v
     a_ms = _ev_time(chunk_append, iters)
     p_ms = _ev_time(prefill, iters)
-    restore_bytes = layers * P * KV_BYTES_PER_TOKEN + P * 4096 * 2 + 24 * (32 * 128 * 128 * 4 + 3 * 8192 * 2)
+    restore_bytes = layers * P * KV_BYTES_PER_TOKEN + P * 4096 * 2 + 24 * (32 * 128 * 128 * 4 + 3 * 8192 * 4)
     flops = layers * 4 * NQ * D * (T * P + T * (T + 1) / 2)
     append_bytes = layers * T * (NQ * D * 2 * 2 + NKV * D * 2 * 4)
     return {"workload": "config2: restore 24576-token prefix (8 layers KV + MTP hidden + 24 GD/conv "
@@ -489,7 +585,7 @@ def bench_config3(capi, iters=10):
     vp = [torch.randn((pages, NKV, PAGE, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
     table = torch.randperm(pages, device="cuda", generator=g).to(torch.int32).view(1, -1)
     live = ([torch.randn(32 * 128 * 128, device="cuda", generator=g) for _ in range(24)]
-            + [torch.randn(3 * 8192, dtype=bf, device="cuda", generator=g) for _ in range(24)])
+            + [torch.randn(3 * 8192, device="cuda", generator=g) for _ in range(24)])
     snap = [torch.empty_like(t) for t in live]
     q_in = [torch.randn((2, NQ, 2 * D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
     k_in = [torch.randn((2, NKV, D), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
@@ -563,6 +659,22 @@ def bench_config3(capi, iters=10):
 
     ms_graph = graph_ms(True)
     ms_two = graph_ms(False)
+    # output check on the last layer: fused vs two calls (bit for bit), two calls vs the oracle
+    seq.fill_(L + 2)
+    lt = layers - 1
+    capi.decode_attn_append(q_in[lt], k_in[lt], v_in[lt], rope, pos, slots, kp[lt], vp[lt], table, seq,
+                            L + 2, SCALE, out, ws, num_queries=2, q_norm_w=qw, k_norm_w=kw, stream=s)
+    out_f = out.clone()
+    capi.append_kv_rope(q_in[lt], q, k_in[lt], v_in[lt], rope, pos, slots, kp[lt], vp[lt],
+                        gate_out=gate, q_norm_w=qw, k_norm_w=kw, stream=s)
+    capi.decode_attn(q, kp[lt], vp[lt], table, seq, L + 2, SCALE, out, ws, num_queries=2, gate=gate,
+                     stream=s)
+    torch.cuda.synchronize()
+    parity = check_decode_against_oracle(capi, [0], q, gate, out, kp[lt], vp[lt], table, seq, nq=2)
+    parity.update(fused_equals_two_calls=bool(torch.equal(out_f, out)),
+                  check="last layer, 2 queries: fused append+decode vs append then decode "
+                        "(bit-exact); decode vs the CPU oracle (abs 2e-2 + rel 1e-2)")
+    parity["ok"] = parity["bad"] == 0 and parity["fused_equals_two_calls"]
     ms = ms_direct if ms_graph is None else min(ms_direct, ms_graph)
     kv = layers * (L + 2) * KV_BYTES_PER_TOKEN
     state = sum(nb)
@@ -575,7 +687,7 @@ def bench_config3(capi, iters=10):
             "ms_per_verify_graph": None if ms_graph is None else round(ms_graph, 3),
             "ms_per_verify_graph_two_calls": None if ms_two is None else round(ms_two, 3),
             "kv_bytes": kv, "state_bytes": state,
-            "GB_s": round(moved / (ms * 1e-3) / 1e9, 1)}
+            "GB_s": round(moved / (ms * 1e-3) / 1e9, 1), "parity": parity}
 
 
 def bench_linear(capi, iters=10):
@@ -772,6 +884,53 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
     ms = timed(step_peer)
     code, _ = capi.device_error()
     ms_nccl = timed(step_nccl)
+    # Output check (last layer of one more step of each path): the peer-exchange output against
+    # the NCCL path's, against every other rank's, and against the oracle, which decodes each
+    # rank's shard on the host into (m, l, o) partials that are gathered and LSE-merged with the
+    # gate. The paths merge in different orders, so they agree to rounding, not bit for bit.
+    import numpy as np
+    from oracle import oracle
+    step_peer()
+    torch.cuda.synchronize()
+    out_peer, q_last, g_last = out.clone(), q.clone(), gate.clone()
+    step_nccl()
+    torch.cuda.synchronize()
+    out_nccl = out.clone()
+    code2, _ = capi.device_error()
+    diff_paths = (out_peer.float() - out_nccl.float()).abs().max().item()
+    if world > 1:
+        outs = [torch.empty_like(out_peer) for _ in range(world)]
+        dist.all_gather(outs, out_peer)
+        ranks_equal = all(torch.equal(o_, outs[0]) for o_ in outs)
+    else:
+        ranks_equal = True
+    oracle.set_threads(max(1, (os.cpu_count() or 1) // world))
+    kp_h, vp_h = _u16(kp[-1]), _u16(vp[-1])
+    tb = np.arange(pages, dtype=np.int32).reshape(1, -1)
+    qh = _u16(q_last).reshape(1, 1, NQ, D)
+    part = oracle.decode_partials_paged(qh, kp_h, vp_h, tb, np.array([n], np.int32), SCALE)[0]
+    del kp_h, vp_h
+    part_t = torch.from_numpy(np.ascontiguousarray(part)).cuda()
+    if world > 1:
+        parts = [torch.empty_like(part_t) for _ in range(world)]
+        dist.all_gather(parts, part_t)
+    else:
+        parts = [part_t]
+    allp = np.ascontiguousarray(torch.stack(parts).cpu().numpy())  # [world][16][258]
+    ref, _ = oracle.merge_partials(allp, NQ, world, NQ * 258, _u16(g_last).reshape(NQ, D).copy())
+    err, bad = _close(_u16(out_peer).reshape(NQ, D), ref)
+    chk = torch.tensor([err, float(bad), diff_paths, float(not ranks_equal), float(code2 != 0)],
+                       dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(chk, op=dist.ReduceOp.MAX)
+    err, bad, diff_paths, ranks_differ, dev_err = chk.tolist()
+    parity = {"check": "last layer: peer-exchange output vs the oracle (per-rank shard partials "
+                       "on the host, gathered, LSE-merged, gated), vs the NCCL path, and across ranks",
+              "tolerance": "abs 2e-2 + rel 1e-2 vs oracle; paths within 1 bf16 ulp",
+              "max_abs_err_vs_oracle": err, "bad_elements": int(bad),
+              "max_abs_diff_peer_vs_nccl": diff_paths, "ranks_identical": ranks_differ == 0,
+              "ranks": world}
+    parity["ok"] = bad == 0 and ranks_differ == 0 and dev_err == 0 and diff_paths <= 1.6e-2
     if world > 1:
         dist.barrier()
     ex.close()
@@ -781,7 +940,7 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
                         f"library's peer-memory exchange kernel (NCCL all-gather path timed beside it)",
             "ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1),
             "GB_s_aggregate": round(kv / (ms * 1e-3) / 1e9, 1), "kv_bytes": kv,
-            "ms_per_token_nccl": round(ms_nccl, 4), "device_error": code}
+            "ms_per_token_nccl": round(ms_nccl, 4), "device_error": code, "parity": parity}
 
 
 # ------------------------------------------------------------------------------ GPU arm
@@ -795,7 +954,7 @@ def run_ours(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     capi.lib()  # fails loudly when the CUDA library is not built
-    lens, layers = workload_lengths(args.workload, rank, args.seed)
+    lens, layers = workload_lengths(args.workload, rank, args.seed, world)
     B = len(lens)
     pages = [(int(L) + 1 + PAGE - 1) // PAGE for L in lens]  # +1: the appended row
     total_pages = sum(pages)
@@ -919,15 +1078,35 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     e2e_ms = e0.elapsed_time(e1)
 
-    t = torch.tensor([ms, e2e_ms, dec_avg], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, dec_avg = (float(x) for x in t.tolist())
+    # Output check of the timed workload, on every rank: layer 0 of this rank's shortest and
+    # longest sequence against the CPU oracle (fp32 accumulate), the gate applied.
+    parity4 = check_decode_against_oracle(
+        capi, [int(np.argmin(lens)), int(np.argmax(lens))], q_rot[0], gate[0], out[0],
+        kpool[0], vpool[0], table, seq_lens)
     total_b, kv_b = step_bytes(lens, layers)
-    tb = torch.tensor([total_b, kv_b, B], dtype=torch.float64, device="cuda")
+    launch_bytes = kv_b / layers + B * NQ * D * 2 * 3  # K/V + q + gate + out of one launch
+    mine = [ms, e2e_ms, dec_avg, float(total_b), float(kv_b), float(B), launch_bytes,
+            float(sum(int(L) for L in lens)), parity4["max_abs_err"], float(parity4["bad"])]
+    t = torch.tensor(mine, dtype=torch.float64, device="cuda")
     if world > 1:
-        dist.all_reduce(tb)
-    all_bytes, all_kv, all_seqs = (float(x) for x in tb.tolist())
+        allr = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allr, t)
+        per_rank = [x.tolist() for x in allr]
+    else:
+        per_rank = [t.tolist()]
+    ms = max(r[0] for r in per_rank)
+    e2e_ms = max(r[1] for r in per_rank)
+    all_bytes = sum(r[3] for r in per_rank)
+    all_seqs = sum(r[5] for r in per_rank)
+    # the dominant kernel's roofline per rank: that rank's launch bytes over its own launch time
+    achieved_rank = [r[6] / (r[2] * 1e-3) / 1e9 for r in per_rank]
+    parity_all = {"config4": {"check": "layer 0 output of each rank's shortest and longest "
+                                       "sequence vs the CPU oracle (fp32 accumulate, gate applied)",
+                              "tolerance": "abs 2e-2 + rel 1e-2",
+                              "max_abs_err": max(r[8] for r in per_rank),
+                              "bad_elements": int(sum(r[9] for r in per_rank)),
+                              "ranks": world}}
+    parity_all["config4"]["ok"] = parity_all["config4"]["bad_elements"] == 0
     cfg5b = None
     if args.workload == "config4" and not args.no_configs:
         kpool.clear()
@@ -940,12 +1119,12 @@ def run_ours(args, rank, world, local_rank):
     value = all_bytes / (step_ms * 1e-3) / 1e9
     e2e_value = all_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
     peak, peak_kind = measured_peaks()
-    # dominant kernel: pgc_decode_attn (split kernel + merge) of one layer on this rank
-    launch_bytes = kv_b / layers + B * NQ * D * 2 * 3  # K/V + q + gate + out
-    achieved = launch_bytes / (dec_avg * 1e-3) / 1e9
+    achieved = min(achieved_rank)
+    dec_avg = per_rank[achieved_rank.index(achieved)][2]
+    launch_bytes = per_rank[achieved_rank.index(achieved)][6]
     traffic = profiled_traffic() if args.workload == "config4" else None
     line = {
-        "metric": "decode-attn achieved HBM GB/s (% of 8 TB/s); decode tok/s",
+        "metric": METRIC,
         "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)",
@@ -960,12 +1139,19 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "tok_s": round(all_seqs / (e2e_ms / args.steps * 1e-3), 1)},
         "roofline": {"bound": "hbm", "kernel": "pgc_decode_attn (decode_split_kernel + merge_kernel)",
+                     "rank_rule": "the slowest rank's launch (min over ranks of own bytes / own time)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": traffic, "launch_ms": round(dec_avg, 4),
                      "algorithmic_bytes_per_launch": launch_bytes},
         "gpu_launches": args.steps * layers * 3,
         "clocks": clk,
+        "per_rank": [{"rank": i, "sequences": int(r[5]), "cached_tokens": int(r[7]),
+                      "step_ms": round(r[0] / args.steps, 4),
+                      "decode_launch_ms": round(r[2], 4),
+                      "decode_launch_GB_s": round(achieved_rank[i], 1)}
+                     for i, r in enumerate(per_rank)],
+        "parity": parity_all,
     }
     if cfg5b is not None:
         line["configs"] = {"config5b": cfg5b}
@@ -973,11 +1159,16 @@ def run_ours(args, rank, world, local_rank):
             line["configs"].update({"config1": bench_config1(capi), "config2": bench_config2(capi),
                                     "config3": bench_config3(capi), "linear": bench_linear(capi),
                                     "q4": bench_q4(capi)})
+    for name, c in line.get("configs", {}).items():
+        if isinstance(c, dict) and "parity" in c:
+            line["parity"][name] = c["parity"]
+    line["parity_ok"] = all(v.get("ok", False) for v in line["parity"].values())
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        gbs, dt, desc = cpu_sample(lens, threads, max_tokens=1 << 30, min_seconds=10.0)
+        sample = CpuSample(lens, threads)
+        gbs, dt, reps = sample.run(min_seconds=10.0, max_layers=layers)
         line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
-                                "kind": "port", "sample": desc + f", {dt:.1f} s"}
+                                "kind": "port", "sample": sample.desc(reps) + f", {dt:.1f} s"}
     print(json.dumps(line), flush=True)
 
 
@@ -1047,7 +1238,7 @@ def profile_kernels(which):
         sv = [torch.randn((NKV, D, stride), dtype=bf, device="cuda", generator=g) for _ in range(layers)]
         sh = torch.randn((P, 4096), dtype=bf, device="cuda", generator=g)
         sgd = [torch.randn(32 * 128 * 128, device="cuda", generator=g) for _ in range(24)]
-        scv = [torch.randn(3 * 8192, dtype=bf, device="cuda", generator=g) for _ in range(24)]
+        scv = [torch.randn(3 * 8192, device="cuda", generator=g) for _ in range(24)]
         kp = [torch.empty((pages, NKV, PAGE, D), dtype=bf, device="cuda") for _ in range(layers)]
         vp = [torch.empty((pages, NKV, PAGE, D), dtype=bf, device="cuda") for _ in range(layers)]
         lh = torch.empty((P + 1600, 4096), dtype=bf, device="cuda")
@@ -1109,15 +1300,6 @@ def main():
         return
     if args.profile_prefill:
         profile_prefill()
-        return
-    if args.only_configs:
-        import torch
-        from peregrine_b200 import capi
-        torch.cuda.set_device(local_rank)
-        print(json.dumps({"configs": {"config1": bench_config1(capi), "config2": bench_config2(capi),
-                                      "config3": bench_config3(capi), "linear": bench_linear(capi),
-                                      "q4": bench_q4(capi),
-                                      "config5b": bench_config5b(capi, 0, 1)}}), flush=True)
         return
     try:
         run_ours(args, rank, world, local_rank)

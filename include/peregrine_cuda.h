@@ -189,12 +189,15 @@ int pgc_decode_attn_append(const uint16_t *q_in, int q_head_stride, const uint16
  * at all: code running where cudaMalloc is unavailable or forbidden (a host whose allocator
  * owns all device memory, a real-time serving loop that bans allocation after start-up, a
  * plugin that is handed only its input and output buffers). The split partials go to a
- * file-scope device array of PGC_DECODE_STATIC_SCRATCH_BYTES that every GPU loading the
- * library keeps until the process exits. Inputs, outputs and their meaning are exactly those
- * of pgc_decode_attn. Returns PGC_ERR_WORKSPACE when pgc_decode_workspace_bytes(batch,
- * num_queries, max_seq_len) exceeds the array. The first call on a device resolves the
- * array's device address (cudaGetSymbolAddress) with that device current: make it before
- * any stream capture. All calls share the array: calls that overlap on the GPU race. Calls
+ * file-scope device array of PGC_DECODE_STATIC_SCRATCH_BYTES per GPU, held until the process
+ * exits. Under CUDA's default lazy module loading the array is reserved on a device when the
+ * library's module is first loaded there, i.e. by the first library call on that device; that
+ * first call also resolves the array's device address (cudaGetSymbolAddress) with the device
+ * current. So make the first call at start-up, before the caller's allocator claims the
+ * device's memory and before any stream capture. Inputs, outputs and their meaning are
+ * exactly those of pgc_decode_attn. Returns PGC_ERR_WORKSPACE when
+ * pgc_decode_workspace_bytes(batch, num_queries, max_seq_len) exceeds the array. All calls
+ * share the array: calls that overlap on the GPU race. Calls
  * no cudaMalloc, cudaFree or allocating library routine. This entry point has no counterpart
  * in the reference. */
 int pgc_decode_attn_static(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,

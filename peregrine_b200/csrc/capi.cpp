@@ -43,22 +43,23 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    // resolved once; a function-local static is initialised exactly once across threads
+    static const EncodeTiledFn fn = []() -> EncodeTiledFn {
         void *p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
                 cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
+            return reinterpret_cast<EncodeTiledFn>(p);
+        return nullptr;
+    }();
     return fn;
 }
 
-int g_sm_count[64] = {0};
-int g_arch_ok[64] = {0};  // 0 unknown, 1 ok, -1 not sm_100
+// per-device facts, cached on first use (atomics: host threads may make first calls at once;
+// racing writers store the same values)
+std::atomic<int> g_sm_count[64] = {};
+std::atomic<int> g_arch_ok[64] = {};  // 0 unknown, 1 ok, -1 not sm_100
 
 int check_device(int *dev_out) {
     int dev = 0;

@@ -669,7 +669,7 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
                           float scale, const uint16_t *gate, uint16_t *out, float *partials_out,
                           void *workspace, int sm_count, cudaStream_t stream,
                           const DecodeAppend *app, int64_t gate_stride) {
-    static bool attr_set[64] = {};  // the attribute is per device context
+    static std::atomic<bool> attr_set[64] = {};  // the attribute is per device context
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
@@ -954,7 +954,7 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
                              const int32_t *seq_len, int max_seq_len, float scale, const uint16_t *gate,
                              uint16_t *out, void *workspace, float *const *bufs, int world, int rank,
                              uint32_t epoch, int sm_count, cudaStream_t stream) {
-    static bool attr_set[64] = {};
+    static std::atomic<bool> attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
@@ -1003,8 +1003,9 @@ cudaError_t decode_read_error(DevErrorHost *e, bool clear) {
 
 // ------------------------------------------------------------------------------------------
 // Allocation-free decode entry (pgc_decode_attn_static). For callers that cannot call
-// cudaMalloc at all, the split partials live in this fixed array, which every GPU that loads
-// the library holds until the process exits. Every call shares it and it keeps the last
+// cudaMalloc at all, the split partials live in this fixed array. A GPU holds it from the
+// library module's load on that device (with CUDA's lazy module loading: the first library
+// call there) until the process exits. Every call shares it and it keeps the last
 // call's contents; nothing in it needs to start at zero, because each call's split kernel
 // writes every partial its merge kernel reads. Two calls that overlap on the GPU (different
 // streams, or different host threads on one device) race on it.

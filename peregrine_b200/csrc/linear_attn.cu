@@ -533,19 +533,6 @@ __device__ __forceinline__ void mma3(float (&d)[4], const uint32_t (&ab)[4], con
 //   phase 2b  S = e^{lg_C} S + (e^{lg_C - lg} delta)^T K   warp w: value rows 16 (w / 4)..,
 //                                                           keys 32 (w % 4)..
 // Shared-memory rows are padded to 4 mod 32 floats, so every fragment read is conflict-free.
-#ifdef PGC_LIN_TRACE
-// Diagnostic build only: clock64 at the scan's phase boundaries, CTA (0, 0), chunk j < 64.
-static __device__ long long g_lin_trace[6][64];
-#define LIN_TRACE(ev, j)                                                                      \
-    do {                                                                                      \
-        if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && (j) < 64)              \
-            g_lin_trace[ev][j] = clock64();                                                   \
-    } while (0)
-#else
-#define LIN_TRACE(ev, j) \
-    do {                 \
-    } while (0)
-#endif
 
 constexpr int kRowsScan = 32;
 constexpr int kDP = kRowsScan + 4;
@@ -621,10 +608,8 @@ __global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *stat
     const int rb = (w >> 2) * 16, kb = (w & 3) * 32;   // phase 2b tile
     for (int c = 0; c < nc; ++c) {
         const int t0 = c * kChunk, n = min(kChunk, T - t0);
-        LIN_TRACE(0, c);
         cp_async_wait<1>();  // A(c) landed (B(c) may still be in flight)
         __syncthreads();
-        LIN_TRACE(1, c);
         // phase 1: dacc = W S^T, qacc = Q S^T over the 128 keys
         float dacc[2][4] = {}, qacc[2][4] = {};
 #pragma unroll 2
@@ -655,7 +640,6 @@ __global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *stat
                 *reinterpret_cast<float2 *>(Dl + i * kDP + col) = make_float2(dacc[nn][2 * h], dacc[nn][2 * h + 1]);
             }
         }
-        LIN_TRACE(2, c);
         __syncthreads();  // W, Q, U released; delta complete
         if (c + 1 < nc) {
             issue_a(c + 1);
@@ -664,7 +648,6 @@ __global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *stat
             cp_async_wait<0>();
         }
         __syncthreads();
-        LIN_TRACE(3, c);
         const float lgC = LGs[n - 1];
         // phase 2a: y = e^{lg} QS + QKm delta (QKm is zero above the diagonal: j <= i0 + 15)
         {
@@ -708,7 +691,6 @@ __global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *stat
                 }
             }
         }
-        LIN_TRACE(4, c);
         __syncthreads();  // the scaled delta is complete
         // phase 2b: S[r][k] = e^{lg_C} S[r][k] + sum_j Dsc[j][r] K[j][k] for this warp's tile
         {
@@ -750,7 +732,6 @@ __global__ void __launch_bounds__(256) gated_delta_chunk_scan_kernel(float *stat
                 *reinterpret_cast<float2 *>(S + (rb + g + 8) * kRowP + col) = make_float2(sacc[nn][2], sacc[nn][3]);
             }
         }
-        LIN_TRACE(5, c);
         __syncthreads();  // K, QKm, lg, delta released
         if (c + 1 < nc) issue_b(c + 1);
     }
@@ -804,7 +785,7 @@ cudaError_t launch_gated_delta_prefill(float *state, int has_state, const uint16
     if (e != cudaSuccess) return e;
     constexpr int kChunkSmem = kChunkSmemFloats * (int)sizeof(float);
     constexpr int kScanSmemC = ScanSmem::kFloats * (int)sizeof(float);
-    static bool attr_set[64] = {};
+    static std::atomic<bool> attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
@@ -820,12 +801,6 @@ cudaError_t launch_gated_delta_prefill(float *state, int has_state, const uint16
     return launch_pdl(gated_delta_chunk_scan_kernel, dim3(kDv / kRowsScan, kHv), dim3(256), kScanSmemC, stream,
                       state, has_state, (const float *)qn, (const float *)kn, (const float *)cw, T, y);
 }
-
-#ifdef PGC_LIN_TRACE
-extern "C" int pgc_debug_lin_trace2(long long *out) {
-    return cudaMemcpyFromSymbol(out, g_lin_trace, sizeof(g_lin_trace)) == cudaSuccess ? 0 : -4;
-}
-#endif
 
 cudaError_t linear_read_error(DevErrorHost *e, bool clear) {
     cudaError_t r = cudaMemcpyFromSymbol(e, g_linear_err, sizeof(DevError));

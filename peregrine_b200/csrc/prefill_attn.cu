@@ -27,29 +27,6 @@ namespace pgc {
 
 PGC_DEFINE_ERROR_WORD(g_prefill_err);
 
-#ifdef PGC_PREFILL_TRACE
-// Diagnostic build only: per-CTA progress of the pair kernel (rank, MMA and softmax steps).
-static __device__ int g_pair_diag[256][8];
-#define PF_DIAG(field, val)                                                                   \
-    do {                                                                                      \
-        const int cid_ = blockIdx.x + blockIdx.y * gridDim.x;                                 \
-        if (cid_ < 256) g_pair_diag[cid_][field] = (val);                                     \
-    } while (0)
-static __device__ long long g_pair_trace[8][512];
-#define PF_TRACE(ev, j)                                                                       \
-    do {                                                                                      \
-        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) < 512)              \
-            g_pair_trace[ev][j] = clock64();                                                  \
-    } while (0)
-#else
-#define PF_TRACE(ev, j) \
-    do {                \
-    } while (0)
-#define PF_DIAG(field, val) \
-    do {                    \
-    } while (0)
-#endif
-
 namespace {
 
 constexpr int kBM = 128;           // rows = 32 tokens x 4 heads
@@ -391,7 +368,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
     cluster_sync_all();  // both CTAs' barriers are initialised before anyone signals them
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (threadIdx.x == 0) PF_DIAG(0, 100 + (int)rank);
     auto leader_addr = [&](uint64_t *bar) { return cluster_map(smem_u32(bar), 0); };
 
     if (warp >= kSoftmaxWarps + 1 && warp < kSoftmaxWarps + 1 + kProducerWarps) {
@@ -490,7 +466,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                     const int pp0 = r0 / kPage, pp1 = min(full_pages, r1 / kPage);
                     const uint32_t vbar = leader_addr(&v_full[sl]);
                     mbar_arrive_expect_tx_cluster(vbar, (uint32_t)max(pp1 - pp0, 0) * 2 * 2048);
-                    PF_DIAG(7, j + 1);
                     for (int pp = pp0; pp < pp1; ++pp) {
                         int page = p.block_table[(key0 >> 4) + pp];
                         if (page < 0 || page >= p.num_pages) {
@@ -533,7 +508,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
             bool ok = wait_or_abort(q_full, 0, abort_flag, 2);
             if (ok) ok = issue_s(0);
             if (ok && n_loc > 1) ok = issue_s(1);
-            PF_DIAG(2, ok ? 1 : -1);
             for (int j = 0; ok && j < n_loc; ++j) {
                 const int b = j & 1;
                 const int sl = j % kVSlotsP;
@@ -542,8 +516,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                     ok = false;
                     break;
                 }
-                PF_DIAG(3, j + 1);
-                PF_TRACE(0, j);
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(smem + Smem2::kV + sl * kVHalf);
 #pragma unroll
@@ -553,9 +525,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                              (j > 0 || kk > 0) ? 1u : 0u);
                 both(&v_empty[sl]);
                 both(&pv_done[b]);
-                PF_TRACE(1, j);
                 if (j + 2 < n_loc) ok = issue_s(j + 2);
-                PF_TRACE(2, j);
             }
         }
     } else {
@@ -583,12 +553,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
             const int b = j & 1;
             if (!wait_or_abort(&s_full[b], (j >> 1) & 1, abort_flag, 6)) { ok = false; break; }
             tc_fence_after();
-            if (threadIdx.x == 0) PF_DIAG(4, j + 1);
-            if (threadIdx.x == 0) PF_TRACE(3, j);
             float sv[32];
             tmem_ld32(tmem + lane_addr + kTS + b * kBNp + cg * 32, sv);
             tmem_wait_ld();
-            if (threadIdx.x == 0) PF_TRACE(5, j);
             const int key0 = (tb + j) * kBNp + cg * 32;
             if (!(key0 + 31 <= vis && row_ok)) {
 #pragma unroll
@@ -607,7 +574,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
             mx = fmaxf(fmaxf(red[r], red[kBM + r]), fmaxf(red[2 * kBM + r], red[3 * kBM + r]));
             // and have read the maxima before the next tile rewrites them
             asm volatile("bar.sync %0, 128;" ::"r"(1 + qd) : "memory");
-            if (threadIdx.x == 0) PF_TRACE(6, j);
             const float m_new = fmaxf(m, mx * c);
             float corr = 1.f;
             if (m_new > m + kLazyRescale) {
@@ -627,7 +593,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
                 pw[i >> 1] = pack_bf16x2(a.x, a.y);
             }
             l = l * corr + (ps2.x + ps2.y);
-            if (threadIdx.x == 0) PF_TRACE(7, j);
             if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
                 if (!wait_or_abort(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 7)) {
                     ok = false;
@@ -654,8 +619,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(pbar[b]);
-            if (threadIdx.x == 0) PF_DIAG(6, j + 1);
-            if (threadIdx.x == 0) PF_TRACE(4, j);
         }
         const int jl = n_loc - 1;
         if (ok && wait_or_abort(&pv_done[jl & 1], (jl >> 1) & 1, abort_flag, 9)) {
@@ -754,7 +717,7 @@ cudaError_t launch_prefill(const uint16_t *q, const CUtensorMap &tk, const CUten
                            int sm_count, cudaStream_t stream) {
     auto kern = prefill_pair_kernel;
     const int smem_bytes = pair::Smem2::kBytes, threads = pair::kThreads, xmul = 2;
-    static bool attr_set[64] = {};
+    static std::atomic<bool> attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
@@ -793,15 +756,3 @@ cudaError_t prefill_read_error(DevErrorHost *e, bool clear) {
 }
 
 }  // namespace pgc
-
-#ifdef PGC_PREFILL_TRACE
-extern "C" int pgc_debug_pair_diag(int *out) {
-    return cudaMemcpyFromSymbol(out, pgc::g_pair_diag, sizeof(int) * 256 * 8) == cudaSuccess ? 0 : -4;
-}
-#endif
-
-#ifdef PGC_PREFILL_TRACE
-extern "C" int pgc_debug_pair_trace(long long *out) {
-    return cudaMemcpyFromSymbol(out, pgc::g_pair_trace, sizeof(long long) * 8 * 512) == cudaSuccess ? 0 : -4;
-}
-#endif

@@ -266,20 +266,6 @@ __device__ __forceinline__ void q4_tmem_ld<16>(uint32_t taddr, float *v) {
 
 PGC_DEFINE_ERROR_WORD(g_q4_err);
 
-#ifdef PGC_Q4_TRACE
-// Diagnostic build only: clock64 of each role's milestones per group in CTA (0, 0, 0).
-static __device__ long long g_q4_trace[10][128];
-#define Q4_TRACE(ev, j)                                                                       \
-    do {                                                                                      \
-        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) < 128)              \
-            g_q4_trace[ev][j] = clock64();                                                    \
-    } while (0)
-#else
-#define Q4_TRACE(ev, j) \
-    do {                \
-    } while (0)
-#endif
-
 __device__ __forceinline__ bool q4_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int where) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
@@ -360,7 +346,6 @@ __global__ void __launch_bounds__(20 * 32, 1)
         return;
     }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) Q4_TRACE(8, 0);
     const int split = blockIdx.x;  // rank in the cluster
     const int o0 = blockIdx.y * 128;
     const int t0 = blockIdx.z * NP;
@@ -410,7 +395,6 @@ __global__ void __launch_bounds__(20 * 32, 1)
     __syncthreads();
     q4_tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (tid == 0) Q4_TRACE(8, 1);
     const uint32_t sbase = smem_u32(q4_smem);
     auto x_slot = [&](int st) { return C::kX + (st % C::kNX) * C::kXStride; };
 
@@ -433,14 +417,12 @@ __global__ void __launch_bounds__(20 * 32, 1)
                 cp_async16_zfill_q4(dst + 16 * u, ok ? src + 8 * u : scales, ok);
             asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
             asm volatile("bar.sync 2, 256;" ::: "memory");
-            if (tid == 0) Q4_TRACE(8, 2);
         }
         const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16) + h * kHalf;
         for (int st = 0; st < nsteps; ++st) {
             const int b = st % C::kTB;
             if (!q4_wait(&tmem_full[b], (st / C::kTB) & 1, abort_flag, 30)) break;
             if (!q4_wait(&xs_full[st % C::kNX], (st / C::kNX) & 1, abort_flag, 31)) break;
-            if (tid == 0) Q4_TRACE(6, st);
             q4_tc_fence_after();
 #pragma unroll
             for (int jg = 0; jg < 2; ++jg) {
@@ -468,7 +450,6 @@ __global__ void __launch_bounds__(20 * 32, 1)
                 mbar_arrive(&tmem_empty[b]);
                 mbar_arrive(&x_empty[st % C::kNX]);
             }
-            if (tid == 0) Q4_TRACE(7, st);
         }
         if (S == 1 && o0 + erow < out_dim) {
 #pragma unroll
@@ -485,10 +466,8 @@ __global__ void __launch_bounds__(20 * 32, 1)
             for (int st = 0; st < nsteps; ++st) {
                 const int bs = st % C::kNB, b = st % C::kTB, xs = st % C::kNX;
                 if (!q4_wait(&conv_full[bs], (st / C::kNB) & 1, abort_flag, 20)) break;
-                Q4_TRACE(3, st);
                 if (!q4_wait(&x_full[xs], (st / C::kNX) & 1, abort_flag, 22)) break;
                 if (!q4_wait(&tmem_empty[b], ((st / C::kTB) & 1) ^ 1, abort_flag, 21)) break;
-                Q4_TRACE(4, st);
                 q4_tc_fence_after();
 #pragma unroll
                 for (int jg = 0; jg < 2; ++jg) {
@@ -502,7 +481,6 @@ __global__ void __launch_bounds__(20 * 32, 1)
                 q4_commit(&bf_empty[bs]);
                 q4_commit(&x_empty[xs]);
                 q4_commit(&tmem_full[b]);
-                Q4_TRACE(5, st);
                 last = st;
             }
             // the tensor cores are done with everything issued before TMEM is released
@@ -516,10 +494,8 @@ __global__ void __launch_bounds__(20 * 32, 1)
         for (int st = 0; st < nsteps; ++st) {
             const int bs = st % C::kNB, ws = st / 2;
             bool ok = q4_wait(&w_full[ws % C::kNW], (ws / C::kNW) & 1, abort_flag, 12);
-            if (c == 0) Q4_TRACE(0, st);
             if (lane == 0 && ok) ok = q4_wait(&bf_empty[bs], ((st / C::kNB) & 1) ^ 1, abort_flag, 10);
             if (__any_sync(0xffffffffu, !ok)) break;
-            if (c == 0) Q4_TRACE(1, st);
             // group j of the W slot: words 4 hh..4 hh+3 are 16-byte chunk 2 j + hh of the row
             const uint8_t *wrow = q4_smem + C::kW + (ws % C::kNW) * 16384 + row * 128;
             uint4 wq[2];
@@ -546,7 +522,6 @@ __global__ void __launch_bounds__(20 * 32, 1)
                 mbar_arrive(&conv_full[bs]);
                 if (st & 1) mbar_arrive(&w_empty[ws % C::kNW]);
             }
-            if (c == 0) Q4_TRACE(2, st);
         }
     } else if (warp < 19) {
         // ------------------------------------------------ x sums: warp 17 + hx, tokens of half hx
@@ -634,7 +609,6 @@ __global__ void __launch_bounds__(20 * 32, 1)
         }
         q4_cluster_sync();  // no CTA leaves while a peer may still read its tile
     }
-    if (tid == 0) Q4_TRACE(8, 3);
     q4_tc_fence_before();
     __syncthreads();
     if (warp == 8) {
@@ -716,17 +690,11 @@ cudaError_t launch_q4_linear(const CUtensorMap &tx, const CUtensorMap &tw, int T
     }
 }
 
-#ifdef PGC_Q4_TRACE
-extern "C" int pgc_debug_q4_trace(long long *out) {
-    return cudaMemcpyFromSymbol(out, g_q4_trace, sizeof(g_q4_trace)) == cudaSuccess ? 0 : -4;
-}
-#endif
-
 cudaError_t launch_q4_gemv(const uint16_t *x, int T, const uint32_t *w, const uint16_t *scales,
                            const uint16_t *biases, uint16_t *y, int out_dim, int in_dim, cudaStream_t stream) {
     const dim3 grid((unsigned)((out_dim + 8 * kGemvRows - 1) / (8 * kGemvRows)));
     const size_t smem = ((size_t)T * in_dim + 2 * 8 * kGemvRows * (in_dim / kQ4Group)) * 2;
-    static bool attr_set[64][kQ4GemvMaxTokens] = {};
+    static std::atomic<bool> attr_set[64][kQ4GemvMaxTokens] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     auto go = [&](auto kernel) {

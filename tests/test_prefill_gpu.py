@@ -41,18 +41,31 @@ def test_prefill_small(cuda, oracle, P, T):
     assert_attn_close(got, ref)
 
 
+def config2_rows(T=1600):
+    """Query rows checked at the config-2 shape: one row in every 64-token pair tile (at a
+    different offset in each, covering both CTAs of a pair), the edges of the first pair and of
+    its two 32-token halves, and the last rows of the chunk (the causal diagonal's end)."""
+    rows = {64 * c + (c * 23) % 64 for c in range(T // 64)}
+    rows |= {0, 1, 31, 32, 63, 64, T - 4, T - 3, T - 2, T - 1}
+    return sorted(r for r in rows if r < T)
+
+
 def test_prefill_config2_shape(cuda, oracle):
-    """BASELINE config 2 attention shape: 1600-token chunk over a 24576-token prefix. Rows are
-    sampled: the first and last 4 tokens against the oracle (the oracle restricted to those
-    query positions), and the last token against the decode kernel over the same cache."""
+    """BASELINE config 2 attention shape: 1600-token chunk over a 24576-token prefix, which the
+    kernel runs as 25 pair tiles x 4 kv heads x 2 key-range shares merged afterwards (every
+    row's keys straddle the share boundary, which sits inside the prefix). Rows of
+    config2_rows() are checked against the oracle restricted to that query position, and the
+    last token against the decode kernel over the same cache."""
     import torch
     P, T = 24576, 1600
+    assert cuda.prefill_workspace_bytes(P, T) == 2 * T * NQ * 258 * 4  # the two-share plan
     q, kp, vp, table = _setup(oracle, P, T, seed=2, spare=0)
     got = _gpu(cuda, q, kp, vp, table, P, T)
-    ref_head, _ = oracle.prefill_paged(np.ascontiguousarray(q[:4]), kp, vp, table, P, 4, SCALE)
-    assert_attn_close(got[:4], ref_head)
-    ref_tail, _ = oracle.prefill_paged(np.ascontiguousarray(q[-4:]), kp, vp, table, P + T - 4, 4, SCALE)
-    assert_attn_close(got[-4:], ref_tail)
+    rows = config2_rows(T)
+    assert len(rows) >= 25 + 8
+    for t in rows:
+        ref, _ = oracle.prefill_paged(np.ascontiguousarray(q[t:t + 1]), kp, vp, table, P + t, 1, SCALE)
+        assert_attn_close(got[t:t + 1], ref)
     n = P + T
     ws = torch.empty(cuda.decode_workspace_bytes(1, 1, n), dtype=torch.uint8, device="cuda")
     out = torch.empty((1, 1, NQ, D), dtype=torch.int16, device="cuda")
