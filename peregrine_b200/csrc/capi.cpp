@@ -326,7 +326,8 @@ int pgc_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_t *
     return cuda_status(launch_decode(q, tk, tv, num_pages, block_tables, max_pages_per_seq, seq_lens,
                                      batch, num_queries, max_seq_len, scale, gate, out, nullptr,
                                      workspace, current_sm_count(),
-                                     static_cast<cudaStream_t>(stream)));
+                                     static_cast<cudaStream_t>(stream), nullptr, PGC_HEAD_DIM,
+                                     k_pages, v_pages));
 }
 
 int pgc_decode_attn_append(const uint16_t *q_in, int q_head_stride, const uint16_t *k_in,
@@ -366,7 +367,7 @@ int pgc_decode_attn_append(const uint16_t *q_in, int q_head_stride, const uint16
     return cuda_status(launch_decode(nullptr, tk, tv, num_pages, block_tables, max_pages_per_seq, seq_lens,
                                      batch, num_queries, max_seq_len, scale, gate, out, nullptr, workspace,
                                      current_sm_count(), static_cast<cudaStream_t>(stream), &app,
-                                     q_head_stride));
+                                     q_head_stride, k_pages, v_pages));
 }
 
 int pgc_decode_attn_static(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
@@ -403,7 +404,8 @@ int pgc_decode_attn_partials(const uint16_t *q, const uint16_t *k_pages,
     return cuda_status(launch_decode(q, tk, tv, num_pages, block_tables, max_pages_per_seq, seq_lens,
                                      batch, num_queries, max_seq_len, scale, nullptr, nullptr,
                                      partials, workspace, current_sm_count(),
-                                     static_cast<cudaStream_t>(stream)));
+                                     static_cast<cudaStream_t>(stream), nullptr, PGC_HEAD_DIM,
+                                     k_pages, v_pages));
 }
 
 int pgc_merge_partials(const float *partials, int64_t rows, int num_parts, int64_t part_stride,

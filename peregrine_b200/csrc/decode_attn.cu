@@ -42,6 +42,8 @@ constexpr int kStageBytes = 2 * kTileBytes;
 constexpr int kQRowBytes = kHeadDim * 2 + 16;  // padded row: conflict-free ldmatrix
 constexpr int kMinPagesPerSplit = 4;
 constexpr int kMaxPagesPerSplit = 64;
+constexpr int kPrefetchPre = 4;    // pages prefetched into L2 before the programmatic-launch wait
+constexpr int kPrefetchAhead = 0;  // pages prefetched past the ring while streaming
 
 struct SplitParams {
     const uint16_t *q;           // rotated query rows, or nullptr with `app` set
@@ -55,6 +57,12 @@ struct SplitParams {
     int pages_per_split;
     int max_splits;
     float scale_log2;
+    // L2 prefetch hints (0: none): `prefetch_pre` pages of this CTA's range are prefetched
+    // before the programmatic-launch wait, from a block-table and length read that may predate
+    // the previous kernel's writes (hints only: the TMA loads after the wait read the pool
+    // coherently through L2); `prefetch_ahead` pages past the ring while streaming.
+    int prefetch_pre, prefetch_ahead;
+    const uint8_t *k_base, *v_base;
 };
 
 struct SmemLayout {
@@ -66,6 +74,11 @@ struct SmemLayout {
     static constexpr int kBytes = kBarOff + (2 * kStages + 1) * 8;  // + kv_ready (fused append)
 };
 constexpr int kSmemBytes = SmemLayout::kBytes + 1024;  // + alignment slack
+
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) from global memory into L2.
+__device__ __forceinline__ void prefetch_l2(const void *ptr, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
+}
 
 template <bool kFused>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -105,6 +118,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (threadIdx.x == kConsumers * 32) {
         tma_prefetch_desc(&tmk);
         tma_prefetch_desc(&tmv);
+        // Start HBM -> L2 traffic for this CTA's first pages while the previous kernel in the
+        // stream drains (its tail and the merge before this launch): page ids outside the pool
+        // are skipped, so a stale table costs bandwidth, never correctness.
+        if (p.prefetch_pre > 0) {
+            const int Lg = p.seq_lens[seq];
+            const int tb = split * p.pages_per_split * kPage;
+            if (tb < Lg) {
+                const int np = min(p.prefetch_pre, (min(Lg, tb + p.pages_per_split * kPage) - tb + kPage - 1) / kPage);
+                const int32_t *tbl = p.block_tables + (int64_t)seq * p.max_pages_per_seq + split * p.pages_per_split;
+                for (int i = 0; i < np; ++i) {
+                    const int pg = tbl[i];
+                    if (pg >= 0 && pg < p.num_pages) {
+                        const int64_t off = ((int64_t)pg * kNumKvHeads + kvh) * kTileBytes;
+                        prefetch_l2(p.k_base + off, kTileBytes);
+                        prefetch_l2(p.v_base + off, kTileBytes);
+                    }
+                }
+            }
+        }
     }
     pdl_wait();
     const int L = p.seq_lens[seq];
@@ -126,7 +158,20 @@ __global__ void __launch_bounds__(kThreads, 2)
                 newpos[j] = (kFused && j < nq) ? p.app.positions[(int64_t)seq * nq + j] : -1;
             const int32_t *table =
                 p.block_tables + (int64_t)seq * p.max_pages_per_seq + split * p.pages_per_split;
+            auto prefetch_page = [&](int i) {
+                const int pg = table[i];
+                if (pg >= 0 && pg < p.num_pages) {
+                    const int64_t off = ((int64_t)pg * kNumKvHeads + kvh) * kTileBytes;
+                    prefetch_l2(p.k_base + off, kTileBytes);
+                    prefetch_l2(p.v_base + off, kTileBytes);
+                }
+            };
+            for (int i = max(kStages, p.prefetch_pre); i < min(n_pages, kStages + p.prefetch_ahead); ++i)
+                prefetch_page(i);
             for (int i = 0; i < n_pages; ++i) {
+                if (i + kStages + p.prefetch_ahead < n_pages && p.prefetch_ahead > 0 &&
+                    i + kStages + p.prefetch_ahead >= p.prefetch_pre)
+                    prefetch_page(i + kStages + p.prefetch_ahead);
                 const int s = i % kStages;
                 const int round = i / kStages;
                 if (round > 0 && !mbar_wait_bounded(&empty[s], (round - 1) & 1)) {
@@ -654,6 +699,11 @@ DecodePlan decode_plan(int batch, int max_seq_len, int sm_count) {
     plan.pages_per_split = (int)pps;
     plan.max_splits = (int)((max_pages + pps - 1) / pps);
     if (plan.max_splits < 1) plan.max_splits = 1;
+    // The pre-wait prefetch pays where one wave of CTAs covers the grid (its ramp then
+    // overlaps the previous kernel's tail); a many-wave grid keeps HBM busy on its own, and
+    // there the extra hints cost bandwidth (config 4: 6388 -> 6251 GB/s with them).
+    plan.prefetch_pre = (int64_t)batch * kNumKvHeads * plan.max_splits <= target_ctas ? kPrefetchPre : 0;
+    plan.prefetch_ahead = kPrefetchAhead;
     return plan;
 }
 
@@ -668,7 +718,8 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
                           const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
                           float scale, const uint16_t *gate, uint16_t *out, float *partials_out,
                           void *workspace, int sm_count, cudaStream_t stream,
-                          const DecodeAppend *app, int64_t gate_stride) {
+                          const DecodeAppend *app, int64_t gate_stride, const void *k_pages,
+                          const void *v_pages) {
     static std::atomic<bool> attr_set[64] = {};  // the attribute is per device context
     int dev = 0;
     cudaGetDevice(&dev);
@@ -695,6 +746,11 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
     sp.pages_per_split = plan.pages_per_split;
     sp.max_splits = plan.max_splits;
     sp.scale_log2 = scale * kLog2e;
+    const bool pf = k_pages != nullptr && v_pages != nullptr;
+    sp.prefetch_pre = pf ? plan.prefetch_pre : 0;
+    sp.prefetch_ahead = pf ? plan.prefetch_ahead : 0;
+    sp.k_base = static_cast<const uint8_t *>(k_pages);
+    sp.v_base = static_cast<const uint8_t *>(v_pages);
     dim3 grid(plan.max_splits, kNumKvHeads, batch);
     cudaError_t le = app != nullptr
                          ? launch_pdl(decode_split_kernel<true>, grid, dim3(kThreads), kSmemBytes, stream, tk, tv, sp)
@@ -964,7 +1020,7 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const DecodePlan plan = decode_plan(1, max_seq_len, sm_count);
-    SplitParams sp;
+    SplitParams sp = {};
     sp.q = q;
     sp.block_tables = block_table;
     sp.seq_lens = seq_len;

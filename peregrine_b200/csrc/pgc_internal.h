@@ -33,6 +33,8 @@ int tiled_map_2d(const void *ptr, int elem_bytes, int64_t inner, int64_t outer, 
 struct DecodePlan {
     int pages_per_split;
     int max_splits;
+    int prefetch_pre;    // L2 prefetch before the programmatic-launch wait, pages per CTA
+    int prefetch_ahead;  // L2 prefetch distance past the ring, pages
 };
 DecodePlan decode_plan(int batch, int max_seq_len, int sm_count);
 size_t decode_workspace_bytes(int batch, int num_queries, int max_seq_len, int sm_count);
@@ -55,7 +57,8 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
                           const int32_t *seq_lens, int batch, int num_queries, int max_seq_len,
                           float scale, const uint16_t *gate, uint16_t *out, float *partials_out,
                           void *workspace, int sm_count, cudaStream_t stream,
-                          const DecodeAppend *app = nullptr, int64_t gate_stride = 256);
+                          const DecodeAppend *app = nullptr, int64_t gate_stride = 256,
+                          const void *k_pages = nullptr, const void *v_pages = nullptr);
 cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_parts,
                                   int64_t part_stride, const uint16_t *gate, uint16_t *out,
                                   cudaStream_t stream);
