@@ -749,7 +749,8 @@ def bench_q4(capi, iters=20):
     1024, o 4096 -> 4096; seeded random packed weights): decode of 64 tokens through
     pgc_q4_linear (bytes = packed weights + scales/biases + activations), and the prefill path
     of a 1600-token chunk: the weights dequantised once by pgc_q4_dequantize (not timed, as the
-    reference prepares its dense RHS once), then a dense bf16 GEMM (cuBLAS through torch)."""
+    reference prepares its dense RHS once), then the library's tcgen05 GEMM (pgc_prefill_linear:
+    q | gate, k and v in one launch, o in another), with cuBLAS (torch.matmul) timed beside it."""
     import torch
     g = torch.Generator(device="cuda")
     g.manual_seed(9)
@@ -785,28 +786,52 @@ def bench_q4(capi, iters=20):
 
     dec_ms, dec_bytes = decode_ms(64)
     one_ms, one_bytes = decode_ms(1)
-    dense = [torch.empty((o, i), dtype=torch.bfloat16, device="cuda") for o, i in shapes]
-    for j in range(4):
-        capi.q4_dequantize(w[0][j], sc[0][j], bi[0][j], dense[j], stream=s)
+    dense = [[torch.empty((o, i), dtype=torch.bfloat16, device="cuda") for o, i in shapes] for _ in range(LAYERS)]
+    for l in range(LAYERS):
+        for j in range(4):
+            capi.q4_dequantize(w[l][j], sc[l][j], bi[l][j], dense[l][j], stream=s)
     Tp = 1600
     xp = torch.randn((Tp, 4096), dtype=torch.bfloat16, device="cuda", generator=g)
+    att = torch.randn((Tp, 4096), dtype=torch.bfloat16, device="cuda", generator=g)
+    yp = [torch.empty((Tp, o), dtype=torch.bfloat16, device="cuda") for o, _ in shapes]
 
     def prefill_step():
-        for _ in range(LAYERS):
-            for j in range(4):
-                torch.matmul(xp, dense[j].t())
+        # per layer: q | gate, k and v share the chunk's hidden rows (one launch); o projects the
+        # attention output
+        for l in range(LAYERS):
+            capi.prefill_linear(xp, dense[l][:3], yp[:3], stream=s)
+            capi.prefill_linear(att, dense[l][3:], yp[3:], stream=s)
 
-    pf_ms = _ev_time(prefill_step, max(2, iters // 4))
+    def prefill_step_cublas():
+        for l in range(LAYERS):
+            for j in range(3):
+                torch.matmul(xp, dense[l][j].t(), out=yp[j])
+            torch.matmul(att, dense[l][3].t(), out=yp[3])
+
+    pf_ms = _ev_time(prefill_step, max(3, iters // 4))
+    pf_cublas_ms = _ev_time(prefill_step_cublas, max(3, iters // 4))
+    # output check: the last layer's four projections against cuBLAS on the same operands
+    prefill_step()
+    ours = [y.clone() for y in yp]
+    prefill_step_cublas()
+    torch.cuda.synchronize()
+    rel = max(float(((a.float() - b.float()).abs().max() / b.float().abs().max()).item())
+              for a, b in zip(ours, yp))
     flops = LAYERS * sum(2 * Tp * o * i for o, i in shapes)
     return {"workload": "q4 projections of 8 full-attention layers: decode of 64 tokens and of 1 token "
-                        "(pgc_q4_linear), prefill of a 1600-token chunk (dequantised weights + cuBLAS "
-                        "bf16 GEMM)",
+                        "(pgc_q4_linear), prefill of a 1600-token chunk (dequantised weights + "
+                        "pgc_prefill_linear tcgen05 GEMM; cuBLAS timed beside it)",
             "decode_ms_per_step": round(dec_ms, 4), "decode_bytes": dec_bytes,
             "decode_GB_s": round(dec_bytes / (dec_ms * 1e-3) / 1e9, 1),
             "decode_1tok_ms_per_step": round(one_ms, 4),
             "decode_1tok_GB_s": round(one_bytes / (one_ms * 1e-3) / 1e9, 1),
             "prefill_ms_per_chunk": round(pf_ms, 3),
-            "prefill_TFLOP_s": round(flops / (pf_ms * 1e-3) / 1e12, 1)}
+            "prefill_TFLOP_s": round(flops / (pf_ms * 1e-3) / 1e12, 1),
+            "prefill_cublas_ms_per_chunk": round(pf_cublas_ms, 3),
+            "prefill_cublas_TFLOP_s": round(flops / (pf_cublas_ms * 1e-3) / 1e12, 1),
+            "parity": {"check": "last layer's q|gate, k, v, o projections: pgc_prefill_linear vs "
+                                "cuBLAS on the same bf16 operands (max |diff| / max |y|)",
+                       "max_rel_diff": rel, "ok": rel < 1e-2}}
 
 
 def bench_config5b(capi, rank, world, iters=20, warmup=3):
@@ -814,7 +839,8 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
     the ranks in contiguous page-aligned KV shards; per layer: q/k RoPE (the new K/V row lands
     on the rank owning position 262144), split-K decode over the local shard, exchange of the
     (m, l, o) partials and LSE merge + gate on every rank. Timed twice: with the library's
-    peer-memory exchange kernel (the reported figure) and with an NCCL all-gather."""
+    peer-memory exchange kernel (the reported figure) and with the library's NCCL path
+    (pgc_cp_decode_attn_nccl: partials, in-place ncclAllGather, merge)."""
     import torch
     import torch.distributed as dist
     from peregrine_b200 import cp
@@ -839,7 +865,6 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
     q = torch.empty((1, NQ, D), dtype=bf, device="cuda")
     gate = torch.empty((1, NQ, D), dtype=bf, device="cuda")
     out = torch.empty((NQ, D), dtype=bf, device="cuda")
-    partial = torch.empty((NQ, 258), dtype=torch.float32, device="cuda")
     gathered = torch.empty((world, NQ, 258), dtype=torch.float32, device="cuda")
     ws = torch.empty(capi.decode_workspace_bytes(1, 1, max(n, 1)), dtype=torch.uint8, device="cuda")
     rope = torch.from_numpy(capi.rope_table(cap)).cuda()
@@ -849,6 +874,7 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
     s = torch.cuda.current_stream()
 
     ex = cp.PeerExchange(world, rank)
+    grp = cp.NcclGroup(world, rank)
 
     def step_peer():
         for l in range(layers):
@@ -861,8 +887,8 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
         for l in range(layers):
             capi.append_kv_rope(q_in[l], q, k_in[l], v_in[l], rope, pos, slot, kp[l], vp[l],
                                 gate_out=gate, stream=s)
-            cp.cp_decode_layer(q.view(1, 1, NQ, D), kp[l], vp[l], table, local_len, n, SCALE,
-                               partial, gathered, ws, out, gate=gate.view(NQ, D), stream=s)
+            grp.decode_layer(q.view(1, 1, NQ, D), kp[l], vp[l], table, local_len, n, SCALE,
+                             gathered, ws, out, gate=gate.view(NQ, D), stream=s)
 
     def timed(step):
         for _ in range(warmup):
@@ -934,10 +960,12 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
     if world > 1:
         dist.barrier()
     ex.close()
+    grp.close()
     kv = layers * cap * KV_BYTES_PER_TOKEN
     return {"workload": f"config5b: one 262144-token sequence, 8 layers, context-parallel over "
                         f"{world} GPU(s) ({n} tokens on rank {rank}); partials exchanged by the "
-                        f"library's peer-memory exchange kernel (NCCL all-gather path timed beside it)",
+                        f"library's peer-memory exchange kernel (the library's NCCL all-gather path, "
+                        f"pgc_cp_decode_attn_nccl, timed beside it)",
             "ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1),
             "GB_s_aggregate": round(kv / (ms * 1e-3) / 1e9, 1), "kv_bytes": kv,
             "ms_per_token_nccl": round(ms_nccl, 4), "device_error": code, "parity": parity}

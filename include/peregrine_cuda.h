@@ -61,7 +61,8 @@ enum pgc_status {
     PGC_ERR_CONTEXT = -8,   /* length outside (0, PGC_MAX_CONTEXT_TOKENS] */
     PGC_ERR_FILE = -9,      /* file missing, unreadable or not writable */
     PGC_ERR_FORMAT = -10,   /* prefix-state file fails validation (wrong model, size, ...) */
-    PGC_ERR_CAPACITY = -11  /* page pool or linear-state slots exhausted after eviction */
+    PGC_ERR_CAPACITY = -11, /* page pool or linear-state slots exhausted after eviction */
+    PGC_ERR_NCCL = -12      /* NCCL missing from the process or an NCCL call failed */
 };
 
 /* Status text for an error code (static storage). */
@@ -70,7 +71,7 @@ const char *pgc_status_string(int status);
 int pgc_version(void);
 /* Reads and optionally clears the device error word of the current device: 0 when no kernel
  * recorded a fault, else code + 100 * unit (units: 0 decode and context-parallel exchange,
- * 1 append, 2 copies, 3 prefill, 4 linear attention, 5 q4 projection). Synchronises the device. Replaces the reference's
+ * 1 append, 2 copies, 3 prefill, 4 linear attention, 5 q4 projection, 6 prefill projection). Synchronises the device. Replaces the reference's
  * MTLCommandBufferStatusError check at commit time (bridge.m:376). */
 int pgc_device_error(int *code_out, int64_t *detail_out, int clear);
 
@@ -554,6 +555,26 @@ int pgc_cp_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_
                        uint16_t *out, void *workspace, size_t workspace_bytes,
                        void *const *buffers, int world, int rank, uint32_t epoch, void *stream);
 
+/* The same context-parallel decode with the partials exchanged by an NCCL all-gather (the
+ * reference is single device; BASELINE config 5b names this collective). One layer:
+ * pgc_decode_attn_partials over the local shard into this rank's slot of `gathered`
+ * ([world][16][258] fp32, device), an in-place ncclAllGather on `stream`, then
+ * pgc_merge_partials with the gate into `out` [16][256] bf16 on every rank. `comm` is an
+ * ncclComm_t of the context-parallel group (rank and size are read from it). NCCL is loaded at
+ * run time (libnccl.so.2, the copy already in the process if any); PGC_ERR_NCCL when it is
+ * missing or a call fails. Setup without another NCCL binding: rank 0 calls
+ * pgc_nccl_get_unique_id, the 128 bytes travel to the other ranks over any host channel, and
+ * every rank calls pgc_nccl_comm_init with its device current; pgc_nccl_comm_destroy at the end. */
+#define PGC_NCCL_UNIQUE_ID_BYTES 128
+int pgc_nccl_get_unique_id(void *id_out);
+int pgc_nccl_comm_init(int world, int rank, const void *id, void **comm_out);
+int pgc_nccl_comm_destroy(void *comm);
+int pgc_cp_decode_attn_nccl(const uint16_t *q, const uint16_t *k_pages, const uint16_t *v_pages,
+                            int64_t num_pages, const int32_t *block_table, int max_pages,
+                            const int32_t *seq_len, int max_seq_len, float scale, const uint16_t *gate,
+                            uint16_t *out, float *gathered, void *workspace, size_t workspace_bytes,
+                            void *comm, void *stream);
+
 /* ---------------------------------------------------------------------------------------
  * q4 (group-64 affine) projections around the attention kernels: weight u32 [out][in/8], 8
  * nibbles per word with the low nibble at the lowest input column; scales and biases bf16
@@ -564,6 +585,19 @@ int pgc_cp_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_
  * prepared dense RHS, src/model/mlx_nt.zig) followed by a dense bf16 GEMM. in_dim % 64 == 0. */
 int pgc_q4_dequantize(const uint32_t *weight, const uint16_t *scales, const uint16_t *biases,
                       uint16_t *out, int out_dim, int in_dim, void *stream);
+
+/* The prefill projections' dense GEMM (src/model/block_attn.zig:96-108: the prepared dense RHS
+ * of each q4 weight, src/model/mlx_nt.zig, multiplied by MLX's NT GEMM, shaders/mlx_gemm.metal):
+ * y_i[t][o] = sum_k x[t][k] * weights_i[o][k] for i < n_weights, fp32 accumulation, bf16
+ * output rounded to nearest. x [tokens][in_dim], weights_i [out_dims[i]][in_dim] (for example
+ * pgc_q4_dequantize's output), outs[i] [tokens][out_dims[i]], all bf16 and 16-byte aligned;
+ * in_dim % 64 == 0, out_dims[i] % 8 == 0, 1 <= n_weights <= PGC_LINEAR_MAX_WEIGHTS. The weights
+ * that share an input (the q | gate, k and v projections) go in one call: their tiles form one
+ * work queue on the tensor cores. Timeouts are recorded in unit 6 of pgc_device_error. */
+#define PGC_LINEAR_MAX_WEIGHTS 4
+int pgc_prefill_linear(const uint16_t *x, int tokens, int in_dim, int n_weights,
+                       const uint16_t *const *weights, const int *out_dims, uint16_t *const *outs,
+                       void *stream);
 
 /* linear_q4_affine_group64_qmv_fast_bf16 (linear.metal:158-194) for decode batches:
  * y[t][o] = sum_k x[t][k] * w[o][k], x [tokens][in] bf16, y [tokens][out] bf16, in fp32 with the

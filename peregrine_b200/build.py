@@ -69,7 +69,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objs = [BUILD / (s.name + ".o") for s in srcs]
     if todo or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc, "-shared", *ARCH, "-o", str(tmp), *map(str, objs), "-lrt"]
+        cmd = [nvcc, "-shared", *ARCH, "-o", str(tmp), *map(str, objs), "-lrt", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

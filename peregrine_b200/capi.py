@@ -32,6 +32,7 @@ STATUS = {
     0: "PGC_OK", -1: "PGC_ERR_INVALID", -2: "PGC_ERR_BOUNDS", -3: "PGC_ERR_WORKSPACE",
     -4: "PGC_ERR_CUDA", -5: "PGC_ERR_ALIGN", -6: "PGC_ERR_DEVICE", -7: "PGC_ERR_TIMEOUT",
     -8: "PGC_ERR_CONTEXT", -9: "PGC_ERR_FILE", -10: "PGC_ERR_FORMAT", -11: "PGC_ERR_CAPACITY",
+    -12: "PGC_ERR_NCCL",
 }
 
 
@@ -136,6 +137,11 @@ SIGNATURES = {
                                  C.c_uint32, P]),
     "pgc_q4_dequantize": (I32, [P, P, P, P, I32, I32, P]),
     "pgc_q4_linear": (I32, [P, I32, P, P, P, P, I32, I32, P]),
+    "pgc_prefill_linear": (I32, [P, I32, I32, I32, P, P, P, P]),
+    "pgc_nccl_get_unique_id": (I32, [P]),
+    "pgc_nccl_comm_init": (I32, [I32, I32, P, P]),
+    "pgc_nccl_comm_destroy": (I32, [P]),
+    "pgc_cp_decode_attn_nccl": (I32, [P, P, P, I64, P, I32, P, I32, F32, P, P, P, P, SZ, P, P]),
     "pgc_page_pool_create": (P, [I32]),
     "pgc_page_pool_destroy": (None, [P]),
     "pgc_page_pool_alloc": (I32, [P, I32, P]),
@@ -449,6 +455,22 @@ def q4_dequantize(weight, scales, biases, out, stream=None) -> None:
     """weight int32/uint32 [out][in/8], scales/biases bf16 [out][in/64] -> out bf16 [out][in]."""
     check(lib().pgc_q4_dequantize(_ptr(weight), _ptr(scales), _ptr(biases), _ptr(out), out.shape[0],
                                   out.shape[1], _stream(stream)), "pgc_q4_dequantize")
+
+
+LINEAR_MAX_WEIGHTS = 4
+
+
+def prefill_linear(x, weights, outs, stream=None) -> None:
+    """pgc_prefill_linear: outs[i] = x @ weights[i]^T (bf16, fp32 accumulate) for the weights that
+    share the input x [tokens][in]; weights[i] bf16 [out_i][in], outs[i] bf16 [tokens][out_i]."""
+    n = len(weights)
+    assert n == len(outs) and 1 <= n <= LINEAR_MAX_WEIGHTS
+    wp = (C.c_void_p * n)(*[w.data_ptr() for w in weights])
+    op = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+    dims = (C.c_int * n)(*[int(w.shape[0]) for w in weights])
+    check(lib().pgc_prefill_linear(_ptr(x), x.shape[0], x.shape[1], n, C.cast(wp, C.c_void_p),
+                                   C.cast(dims, C.c_void_p), C.cast(op, C.c_void_p), _stream(stream)),
+          "pgc_prefill_linear")
 
 
 def q4_linear(x, weight, scales, biases, y, stream=None) -> None:

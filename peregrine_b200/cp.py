@@ -9,9 +9,12 @@ HBM or latency budget (BASELINE config 5b): rank g holds the contiguous, page-al
   3. pgc_merge_partials: the log-sum-exp combine of attention_decode.metal:215-243 applied to
      the gathered shard partials, optional sigmoid gate, bf16 output on every rank.
 The new token's K/V row is appended only on the rank owning its position (the tail shard).
-Two exchange paths: `cp_decode_layer` all-gathers the partials through torch.distributed (NCCL),
-and `PeerExchange.decode_layer` moves them with the library's own exchange kernel over NVLink
-peer memory (merge, stores into every rank's buffer, epoch flags, final merge in one kernel).
+Three exchange paths: `NcclGroup.decode_layer` runs the library's NCCL path
+(pgc_cp_decode_attn_nccl: partials, in-place ncclAllGather, merge, all behind the C ABI, on a
+communicator the library creates), `cp_decode_layer` all-gathers through torch.distributed (the
+same steps composed in Python), and `PeerExchange.decode_layer` moves the partials with the
+library's own exchange kernel over NVLink peer memory (merge, stores into every rank's buffer,
+epoch flags, final merge in one kernel).
 """
 from __future__ import annotations
 
@@ -110,6 +113,45 @@ class PeerExchange:
             max(local_max_len, 1), scale, None if gate is None else gate.data_ptr(), out.data_ptr(),
             workspace.data_ptr(), workspace.numel() * workspace.element_size(), self.buffers,
             self.world, self.rank, self.epoch, capi._stream(stream)), "pgc_cp_decode_attn")
+
+
+class NcclGroup:
+    """An NCCL communicator of the context-parallel group, made through the library's C ABI:
+    rank 0 draws the unique id (pgc_nccl_get_unique_id), the 128 bytes travel over the process
+    group as a host object, and every rank joins with pgc_nccl_comm_init on its current device.
+    A host without torch does the same with any channel for the id."""
+
+    def __init__(self, world: int, rank: int, group=None):
+        import ctypes as C
+
+        import torch.distributed as dist
+        self.world, self.rank = world, rank
+        uid = (C.c_uint8 * 128)()
+        if rank == 0:
+            capi.check(capi.lib().pgc_nccl_get_unique_id(uid), "pgc_nccl_get_unique_id")
+        if world > 1:
+            obj = [bytes(uid)]
+            dist.broadcast_object_list(obj, src=0, group=group)
+            uid = (C.c_uint8 * 128).from_buffer_copy(obj[0])
+        comm = C.c_void_p()
+        capi.check(capi.lib().pgc_nccl_comm_init(world, rank, uid, C.byref(comm)), "pgc_nccl_comm_init")
+        self.comm = comm.value
+
+    def close(self) -> None:
+        if self.comm:
+            capi.check(capi.lib().pgc_nccl_comm_destroy(self.comm), "pgc_nccl_comm_destroy")
+            self.comm = None
+
+    def decode_layer(self, q, k_pages, v_pages, block_table, local_len_dev, local_max_len, scale,
+                     gathered, workspace, out, gate=None, stream=None) -> None:
+        """One layer for one query token: partials of the local shard, in-place all-gather into
+        gathered [world, 16, 258] fp32, merge + gate into out [16, 256] bf16 on every rank."""
+        capi.check(capi.lib().pgc_cp_decode_attn_nccl(
+            q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), k_pages.shape[0],
+            block_table.data_ptr(), block_table.shape[-1], local_len_dev.data_ptr(),
+            max(local_max_len, 1), scale, None if gate is None else gate.data_ptr(), out.data_ptr(),
+            gathered.data_ptr(), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+            self.comm, capi._stream(stream)), "pgc_cp_decode_attn_nccl")
 
 
 def cp_decode_layer(q, k_pages, v_pages, block_table, local_len_dev, local_max_len, scale,

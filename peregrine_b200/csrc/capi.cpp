@@ -210,6 +210,7 @@ const char *pgc_status_string(int status) {
         case PGC_ERR_FILE: return "file missing or not accessible";
         case PGC_ERR_FORMAT: return "prefix-state file failed validation";
         case PGC_ERR_CAPACITY: return "page pool or state slots exhausted";
+        case PGC_ERR_NCCL: return "NCCL unavailable or an NCCL call failed";
         default: return "unknown status";
     }
 }
@@ -220,17 +221,18 @@ int pgc_device_error(int *code_out, int64_t *detail_out, int clear) {
     int st = check_device(nullptr);
     if (st != PGC_OK) return st;
     if (cudaDeviceSynchronize() != cudaSuccess) return PGC_ERR_CUDA;
-    DevErrorHost e[6] = {};
+    DevErrorHost e[7] = {};
     cudaError_t r = decode_read_error(&e[0], clear != 0);
     if (r == cudaSuccess) r = append_read_error(&e[1], clear != 0);
     if (r == cudaSuccess) r = copy_read_error(&e[2], clear != 0);
     if (r == cudaSuccess) r = prefill_read_error(&e[3], clear != 0);
     if (r == cudaSuccess) r = linear_read_error(&e[4], clear != 0);
     if (r == cudaSuccess) r = q4_read_error(&e[5], clear != 0);
+    if (r == cudaSuccess) r = prefill_linear_read_error(&e[6], clear != 0);
     if (r != cudaSuccess) return PGC_ERR_CUDA;
     int code = 0;
     long long detail = 0;
-    for (int i = 0; i < 6 && code == 0; ++i)
+    for (int i = 0; i < 7 && code == 0; ++i)
         if (e[i].code != 0) {
             code = e[i].code + 100 * i;  // unit in the hundreds digit
             detail = e[i].detail;
@@ -735,6 +737,33 @@ int pgc_q4_linear(const uint16_t *x, int tokens, const uint32_t *weight, const u
     if ((st = tiled_map_2d(weight, 4, in_dim / 8, out_dim, 32, 128, true, &tw)) != PGC_OK) return st;
     return cuda_status(launch_q4_linear(tx, tw, tokens, scales, biases, y, out_dim, in_dim,
                                         static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_prefill_linear(const uint16_t *x, int tokens, int in_dim, int n_weights,
+                       const uint16_t *const *weights, const int *out_dims, uint16_t *const *outs,
+                       void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (tokens < 0 || in_dim <= 0 || in_dim % 64 != 0 || n_weights < 1 ||
+        n_weights > PGC_LINEAR_MAX_WEIGHTS || !weights || !out_dims || !outs)
+        return PGC_ERR_INVALID;
+    for (int i = 0; i < n_weights; ++i) {
+        if (!weights[i] || !outs[i] || out_dims[i] <= 0 || out_dims[i] % 8 != 0) return PGC_ERR_INVALID;
+        if (!al16(weights[i]) || !al16(outs[i])) return PGC_ERR_ALIGN;
+    }
+    if (tokens == 0) return PGC_OK;
+    if (!x) return PGC_ERR_INVALID;
+    if (!al16(x)) return PGC_ERR_ALIGN;
+    CUtensorMap tx, tw[PGC_LINEAR_MAX_WEIGHTS];
+    LinearOut lo[PGC_LINEAR_MAX_WEIGHTS];
+    if ((st = tiled_map_2d(x, 2, in_dim, tokens, 64, 128, true, &tx)) != PGC_OK) return st;
+    for (int i = 0; i < n_weights; ++i) {
+        if ((st = tiled_map_2d(weights[i], 2, in_dim, out_dims[i], 64, 128, true, &tw[i])) != PGC_OK) return st;
+        lo[i].y = outs[i];
+        lo[i].out_dim = out_dims[i];
+    }
+    return cuda_status(launch_prefill_linear(tx, tw, lo, n_weights, tokens, in_dim, current_sm_count(),
+                                             static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

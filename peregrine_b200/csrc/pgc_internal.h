@@ -144,4 +144,15 @@ cudaError_t launch_q4_gemv(const uint16_t *x, int T, const uint32_t *w, const ui
                            const uint16_t *biases, uint16_t *y, int out_dim, int in_dim, cudaStream_t stream);
 cudaError_t q4_read_error(DevErrorHost *e, bool clear);
 
+// prefill_linear.cu
+struct LinearOut {
+    uint16_t *y;
+    int out_dim;
+};
+// x: [T][in_dim] bf16 (64 x 128 boxes, 128-byte swizzle); tw[i]: weight i [out_dim][in_dim]
+// (same boxes). in_dim % 64 == 0, out_dim % 8 == 0.
+cudaError_t launch_prefill_linear(const CUtensorMap &tx, const CUtensorMap *tw, const LinearOut *outs,
+                                  int n_weights, int T, int in_dim, int sm_count, cudaStream_t stream);
+cudaError_t prefill_linear_read_error(DevErrorHost *e, bool clear);
+
 }  // namespace pgc

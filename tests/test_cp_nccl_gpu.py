@@ -1,5 +1,7 @@
 """Context-parallel decode on 2 GPUs through the library: each rank holds one KV shard on its
-own GPU. Two exchange paths: pgc_decode_attn_partials + NCCL all-gather + pgc_merge_partials,
+own GPU. Three exchange paths: pgc_cp_decode_attn_nccl (partials, in-place ncclAllGather and
+merge behind the C ABI, on a communicator made by pgc_nccl_comm_init), the same steps composed
+through torch.distributed (pgc_decode_attn_partials + all-gather + pgc_merge_partials),
 and pgc_cp_decode_attn, whose exchange kernel stores the partials into the peers' buffers over
 NVLink and waits on epoch flags. Every rank's output must match the oracle over the whole cache
 within the attention tolerance (2e-2 abs + 1e-2 rel). Skipped when fewer than 2 GPUs are
@@ -22,7 +24,7 @@ def _free_port():
     return port
 
 
-def _rank_main(rank, world, port, L, result_dir, fused=False):
+def _rank_main(rank, world, port, L, result_dir, path="torch"):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     import torch
@@ -57,7 +59,14 @@ def _rank_main(rank, world, port, L, result_dir, fused=False):
         gathered = torch.empty((world, NQ, 258), dtype=torch.float32, device="cuda")
         ws = torch.empty(capi.decode_workspace_bytes(1, 1, max(n, 1)), dtype=torch.uint8, device="cuda")
         out = torch.empty((NQ, D), dtype=torch.int16, device="cuda")
-        if fused:
+        if path == "capi_nccl":
+            grp = cp.NcclGroup(world, rank)
+            for _ in range(3):  # several layers on one communicator
+                grp.decode_layer(dv(q), dv(kp), dv(vp), table, dv(np.array([n], np.int32)), n, 1 / 16,
+                                 gathered, ws, out, gate=dv(g))
+            torch.cuda.synchronize()
+            grp.close()
+        elif path == "peer":
             ex = cp.PeerExchange(world, rank)
             dist.barrier()
             # several layers in a row: exercises the epoch parity double buffer
@@ -88,15 +97,15 @@ def _rank_main(rank, world, port, L, result_dir, fused=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fused", [False, True], ids=["nccl", "peer"])
+@pytest.mark.parametrize("path", ["capi_nccl", "torch", "peer"])
 @pytest.mark.parametrize("L", [5000, 16])
-def test_cp_decode_two_gpus(tmp_path, L, fused):
+def test_cp_decode_two_gpus(tmp_path, L, path):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     world = 2
-    mp.start_processes(_rank_main, args=(world, _free_port(), L, str(tmp_path), fused), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, _free_port(), L, str(tmp_path), path), nprocs=world,
                        join=True, start_method="spawn")
     for r in range(world):
         ok, err = np.load(tmp_path / f"rank{r}.npy")
