@@ -50,9 +50,11 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1-3 side figures")
-    ap.add_argument("--profile-kernels", choices=["q4", "linear", "restore", "verify"], default=None,
+    ap.add_argument("--profile-kernels", choices=["q4", "linear", "restore", "verify", "projection"],
+                    default=None,
                     help="small cases for ncu captures: the q4 decode projection, the gated-delta "
-                         "prefill, the config-2 restore, one config-3 verify layer (fused and two-call)")
+                         "prefill, the config-2 restore, one config-3 verify layer (fused and two-call), "
+                         "one layer's prefill projections")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="profiling aid: config 2's causal prefill on one layer, 3 launches")
     return ap.parse_args()
@@ -1305,6 +1307,16 @@ def profile_kernels(which):
             capi.append_kv_rope(q_in, q, k_in, v_in, rope, pos, slots, kp, vp, gate_out=gate, q_norm_w=qw,
                                 k_norm_w=kw)
             capi.decode_attn(q, kp, vp, table, seq, L + 2, SCALE, out, ws, num_queries=2, gate=gate)
+    elif which == "projection":
+        # one layer's prefill projections at a 1600-token chunk (q | gate, k, v in one launch, then
+        # o), 3 times: 117 MB of bf16 weights, about 0.2 GB on the device
+        T, i = 1600, 4096
+        ws = [torch.randn((o, i), dtype=bf, device="cuda", generator=g) for o in (8192, 1024, 1024, 4096)]
+        x = torch.randn((T, i), dtype=bf, device="cuda", generator=g)
+        ys = [torch.empty((T, w.shape[0]), dtype=bf, device="cuda") for w in ws]
+        for _ in range(3):
+            capi.prefill_linear(x, ws[:3], ys[:3])
+            capi.prefill_linear(x, ws[3:], ys[3:])
     torch.cuda.synchronize()
     print(json.dumps({"profile": which}), flush=True)
 
