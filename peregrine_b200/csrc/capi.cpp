@@ -700,7 +700,8 @@ int pgc_cp_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_
     if ((st = pool_tensor_map(v_pages, num_pages, &tv)) != PGC_OK) return st;
     return cuda_status(launch_cp_decode(q, tk, tv, num_pages, block_table, max_pages, seq_len, max_seq_len,
                                         scale, gate, out, workspace, bufs, world, rank, epoch,
-                                        current_sm_count(), static_cast<cudaStream_t>(stream)));
+                                        current_sm_count(), static_cast<cudaStream_t>(stream), k_pages,
+                                        v_pages));
 }
 
 // ------------------------------------------------------------------ q4 projections

@@ -694,7 +694,10 @@ DecodePlan decode_plan(int batch, int max_seq_len, int sm_count) {
     const int64_t target_ctas = (int64_t)sm_count * 2;
     int64_t pps = (units + target_ctas - 1) / target_ctas;
     if (pps < kMinPagesPerSplit) pps = kMinPagesPerSplit;
-    if (pps > kMaxPagesPerSplit) pps = kMaxPagesPerSplit;
+    // The cap keeps a ragged batch's longest sequence from stretching the wave; one sequence has
+    // no such spread, so its splits grow until one wave covers it (a 262144-token context-parallel
+    // shard: 74 splits of 222 pages per kv head instead of 257 of 64).
+    if (pps > kMaxPagesPerSplit && batch > 1) pps = kMaxPagesPerSplit;
     DecodePlan plan;
     plan.pages_per_split = (int)pps;
     plan.max_splits = (int)((max_pages + pps - 1) / pps);
@@ -813,14 +816,16 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
 // KV shard of a long sequence; the split kernel leaves its per-split partials in the
 // workspace. The exchange kernel (one CTA per row and 32-dim chunk) then (1) LSE-merges those splits into the
 // rank's partial (16 rows x (m, l, o[256])), (2) stores it straight into every rank's exchange
-// buffer over NVLink, (3) publishes an epoch flag in each rank's buffer (release at system
-// scope), (4) waits for every rank's flag in its own buffer (acquire, bounded) and (5) merges the
-// world partials with the gate into the bf16 output. This replaces merge kernel + all-gather + merge kernel:
-// launched right behind the split kernel (programmatic dependent launch), it is resident when
-// the last split finishes. Exchange buffer per rank: [2 parities][world][16][258] f32, then
-// world u32 flags at cp_flags_offset and a u32 CTA counter 128 bytes after them. Parity epoch & 1 double-buffers the slots: rank r cannot
-// start call e + 2 before every rank has published e + 1, which each does only after finishing
-// its reads of call e.
+// buffer over NVLink, (3) counts its arrival in each rank's buffer (a release add at system
+// scope on the counter of its source rank), (4) waits until every source rank's counter in its
+// own buffer has counted all 128 CTAs of this call (acquire, bounded) and (5) merges the world
+// partials with the gate into the bf16 output. This replaces merge kernel + all-gather + merge
+// kernel: launched right behind the split kernel (programmatic dependent launch), it is resident
+// when the last split finishes. Exchange buffer per rank: [2 parities][world][16][258] f32, then
+// world u64 arrival counters at cp_flags_offset. The counters only grow (call e is complete
+// from every source at e * 128), so they need no reset; the buffer starts zeroed. Parity
+// epoch & 1 double-buffers the slots: rank r cannot start call e + 2 before every rank has
+// counted in for e + 1, which each does only after finishing its reads of call e.
 constexpr int kCpRows = kNumQHeads;
 
 struct CpParams {
@@ -835,23 +840,21 @@ struct CpParams {
     uint16_t *out;
 };
 
-__device__ __forceinline__ uint32_t *cp_flags(float *buf, int world) {
-    return reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(buf) + cp_flags_offset(world));
+__device__ __forceinline__ unsigned long long *cp_counters(float *buf, int world) {
+    return reinterpret_cast<unsigned long long *>(reinterpret_cast<uint8_t *>(buf) + cp_flags_offset(world));
 }
 
 // One CTA per (row, 32-dim chunk), 128 CTAs: the 8 warps stride over the local splits (lane =
 // dim), as the merge kernel does, so the L2 reads of up to 256 split partials per row overlap.
-// Each CTA stores its slice of the row partial (chunk 0 also m and l) into every rank's buffer
-// over NVLink, fences at system scope and counts itself in this rank's buffer; the last CTA
-// publishes the epoch flag to every rank. Every CTA then waits for all ranks' flags and merges
-// its slice over the world partials.
+// Warp w stores the CTA's slice of the row partial (chunk 0 also m and l) into rank w's buffer
+// over NVLink, fences at system scope and adds one to rank w's counter for this source rank.
+// Every CTA then waits for all ranks' counters and merges its slice over the world partials.
 constexpr int kCpCtas = kCpRows * (kHeadDim / 32);
 
 __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
     pdl_trigger();
     pdl_wait();
     __shared__ float wm[8], wden[8], wacc[8][32];
-    __shared__ int last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r = blockIdx.x, d0 = blockIdx.y * 32;
     const int L = *p.seq_len;
@@ -934,7 +937,8 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
         }
         return;
     }
-    // this CTA's slice of the rank partial -> every rank's slot [parity][rank][r]
+    // this CTA's slice of the rank partial -> every rank's slot [parity][rank][r], then one
+    // arrival on that rank's counter for this source rank
     const int parity = (int)(p.epoch & 1u);
     if (warp < p.world) {
         float *dst = p.bufs[warp] + (((int64_t)parity * p.world + p.rank) * kCpRows + r) * kPartial;
@@ -949,29 +953,21 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
             dst[0] = ma;
             dst[1] = sden;
         }
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (tid == 0) {
-        unsigned int *count = reinterpret_cast<unsigned int *>(cp_flags(p.bufs[p.rank], p.world) + 32);
-        last = atomicAdd(count, 1u) == (unsigned)(kCpCtas - 1);
-        if (last) {
-            atomicExch(count, 0u);  // ready for the next call
-            __threadfence_system();
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0) {
+            unsigned long long *ctr = cp_counters(p.bufs[warp], p.world) + p.rank;
+            asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(ctr), "l"(1ull) : "memory");
         }
     }
-    __syncthreads();
-    if (last && tid < p.world) {
-        uint32_t *f = cp_flags(p.bufs[tid], p.world) + p.rank;
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(p.epoch) : "memory");
-    }
     if (tid < p.world) {
-        const uint32_t *f = cp_flags(p.bufs[p.rank], p.world) + tid;
+        const unsigned long long *ctr = cp_counters(p.bufs[p.rank], p.world) + tid;
+        const unsigned long long target = (unsigned long long)p.epoch * kCpCtas;
         const uint64_t t0 = global_timer_ns();
         for (uint32_t it = 0;; ++it) {
-            uint32_t v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-            if ((int32_t)(v - p.epoch) >= 0) break;
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ctr) : "memory");
+            if (v >= target) break;
             if ((it & 63u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
                 record_error(&g_decode_err, kErrWaitTimeout, 1000 + tid);
                 break;
@@ -1009,7 +1005,8 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
                              int64_t num_pages, const int32_t *block_table, int max_pages,
                              const int32_t *seq_len, int max_seq_len, float scale, const uint16_t *gate,
                              uint16_t *out, void *workspace, float *const *bufs, int world, int rank,
-                             uint32_t epoch, int sm_count, cudaStream_t stream) {
+                             uint32_t epoch, int sm_count, cudaStream_t stream, const void *k_pages,
+                             const void *v_pages) {
     static std::atomic<bool> attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1031,6 +1028,11 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
     sp.pages_per_split = plan.pages_per_split;
     sp.max_splits = plan.max_splits;
     sp.scale_log2 = scale * kLog2e;
+    const bool pf = k_pages != nullptr && v_pages != nullptr;
+    sp.prefetch_pre = pf ? plan.prefetch_pre : 0;
+    sp.prefetch_ahead = pf ? plan.prefetch_ahead : 0;
+    sp.k_base = static_cast<const uint8_t *>(k_pages);
+    sp.v_base = static_cast<const uint8_t *>(v_pages);
     cudaError_t e = launch_pdl(decode_split_kernel<false>, dim3(plan.max_splits, kNumKvHeads, 1), dim3(kThreads),
                                kSmemBytes, stream, tk, tv, sp);
     if (e != cudaSuccess) return e;

@@ -72,7 +72,8 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
                              int64_t num_pages, const int32_t *block_table, int max_pages,
                              const int32_t *seq_len, int max_seq_len, float scale, const uint16_t *gate,
                              uint16_t *out, void *workspace, float *const *bufs, int world, int rank,
-                             uint32_t epoch, int sm_count, cudaStream_t stream);
+                             uint32_t epoch, int sm_count, cudaStream_t stream,
+                             const void *k_pages = nullptr, const void *v_pages = nullptr);
 int decode_static_scratch(void **ptr_out);
 
 // kv_append.cu

@@ -149,9 +149,10 @@ def test_host_validation(cuda):
 
 
 def test_single_long_sequence_merge_over_80_parts(cuda, oracle):
-    """One 100000-token sequence: 98 key-range splits, more than the merge keeps in registers
-    (80 per row), so the merge takes its streaming path."""
-    lens = [100000]
+    """A 100000-token sequence beside a short one: the batch's splits are capped at 64 pages, so
+    the long row has 98 key-range splits, more than the merge keeps in registers (80 per row),
+    and the merge takes its streaming path."""
+    lens = [100000, 3000]
     q, kp, vp, table, seq, g = _case(oracle, lens, seed=11, gate=True, spare_pages=0)
     got = _run(cuda, q, kp, vp, table, seq, 1, g)
     ref, _ = oracle.decode_paged(q, kp, vp, table, seq, SCALE, 1, g)
@@ -178,3 +179,13 @@ def test_merge_partials_part_counts(cuda, oracle, num_parts):
     cuda.merge_partials(torch.from_numpy(parts).cuda(), rows, num_parts, rows * 258, out, gate=dev(g))
     torch.cuda.synchronize()
     assert_attn_close(host_u16(out).reshape(1, 1, rows, D), ref.reshape(1, 1, rows, D))
+
+
+def test_single_sequence_one_wave_long_splits(cuda, oracle):
+    """One 150000-token sequence alone: its splits are not capped (a one-wave plan of long
+    splits, over 64 pages each)."""
+    lens = [150000]
+    q, kp, vp, table, seq, g = _case(oracle, lens, seed=12, gate=True, spare_pages=0)
+    got = _run(cuda, q, kp, vp, table, seq, 1, g)
+    ref, _ = oracle.decode_paged(q, kp, vp, table, seq, SCALE, 1, g)
+    assert_attn_close(got, ref)
