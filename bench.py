@@ -770,12 +770,14 @@ def bench_q4(capi, iters=20):
         ys = [torch.empty((T, o), dtype=torch.bfloat16, device="cuda") for o, _ in shapes]
 
         def decode_step():
+            # per layer: q | gate, k and v share x (pgc_q4_linear_multi: one launch at 1-2
+            # tokens), then o
             st = torch.cuda.current_stream()
             for l in range(LAYERS):
-                for j in range(4):
-                    capi.q4_linear(x, w[l][j], sc[l][j], bi[l][j], ys[j], stream=st)
+                capi.q4_linear_multi(x, w[l][:3], sc[l][:3], bi[l][:3], ys[:3], stream=st)
+                capi.q4_linear(x, w[l][3], sc[l][3], bi[l][3], ys[3], stream=st)
 
-        # 32 small launches per step: replayed as one CUDA graph, so the figure is device time
+        # 16 (1-2 tokens) or 32 small launches per step: replayed as one CUDA graph, so the figure is device time
         # and not the Python launch rate
         decode_step()
         torch.cuda.synchronize()

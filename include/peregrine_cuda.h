@@ -610,6 +610,15 @@ int pgc_prefill_linear(const uint16_t *x, int tokens, int in_dim, int n_weights,
 int pgc_q4_linear(const uint16_t *x, int tokens, const uint32_t *weight, const uint16_t *scales,
                   const uint16_t *biases, uint16_t *y, int out_dim, int in_dim, void *stream);
 
+/* pgc_q4_linear for up to PGC_LINEAR_MAX_WEIGHTS weights that share the input x (the q | gate, k
+ * and v projections of a decode step, block_attn.zig:309-320): outs[i] = x w_i^T with the same
+ * algebra and rules per weight. At 1-2 tokens all of them run as one launch of the CUDA-core
+ * GEMV (their row blocks form one grid); at more tokens each weight is its own tensor-core pass. */
+int pgc_q4_linear_multi(const uint16_t *x, int tokens, int in_dim, int n_weights,
+                        const uint32_t *const *weights, const uint16_t *const *scales,
+                        const uint16_t *const *biases, uint16_t *const *outs, const int *out_dims,
+                        void *stream);
+
 #ifdef __cplusplus
 }
 #endif

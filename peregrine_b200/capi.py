@@ -138,6 +138,7 @@ SIGNATURES = {
     "pgc_q4_dequantize": (I32, [P, P, P, P, I32, I32, P]),
     "pgc_q4_linear": (I32, [P, I32, P, P, P, P, I32, I32, P]),
     "pgc_prefill_linear": (I32, [P, I32, I32, I32, P, P, P, P]),
+    "pgc_q4_linear_multi": (I32, [P, I32, I32, I32, P, P, P, P, P, P]),
     "pgc_nccl_get_unique_id": (I32, [P]),
     "pgc_nccl_comm_init": (I32, [I32, I32, P, P]),
     "pgc_nccl_comm_destroy": (I32, [P]),
@@ -471,6 +472,20 @@ def prefill_linear(x, weights, outs, stream=None) -> None:
     check(lib().pgc_prefill_linear(_ptr(x), x.shape[0], x.shape[1], n, C.cast(wp, C.c_void_p),
                                    C.cast(dims, C.c_void_p), C.cast(op, C.c_void_p), _stream(stream)),
           "pgc_prefill_linear")
+
+
+def q4_linear_multi(x, weights, scales, biases, ys, stream=None) -> None:
+    """pgc_q4_linear_multi: ys[i] = x @ w_i^T for the q4 weights that share x [tokens][in]."""
+    n = len(weights)
+    assert n == len(scales) == len(biases) == len(ys) and 1 <= n <= LINEAR_MAX_WEIGHTS
+
+    def arr(ts):
+        return C.cast((C.c_void_p * n)(*[t.data_ptr() for t in ts]), C.c_void_p)
+
+    dims = (C.c_int * n)(*[int(y.shape[1]) for y in ys])
+    check(lib().pgc_q4_linear_multi(_ptr(x), x.shape[0], x.shape[1], n, arr(weights), arr(scales),
+                                    arr(biases), arr(ys), C.cast(dims, C.c_void_p), _stream(stream)),
+          "pgc_q4_linear_multi")
 
 
 def q4_linear(x, weight, scales, biases, y, stream=None) -> None:

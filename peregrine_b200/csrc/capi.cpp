@@ -729,15 +729,48 @@ int pgc_q4_linear(const uint16_t *x, int tokens, const uint32_t *weight, const u
     if (!x || !weight || !scales || !biases || !y) return PGC_ERR_INVALID;
     if (!al16(x) || !al16(weight) || !al16(scales) || !al16(biases) || ((uintptr_t)y & 1u) != 0)
         return PGC_ERR_ALIGN;
-    if (tokens <= kQ4GemvMaxTokens)
-        return cuda_status(launch_q4_gemv(x, tokens, weight, scales, biases, y, out_dim, in_dim,
-                                          static_cast<cudaStream_t>(stream)));
+    if (tokens <= kQ4GemvMaxTokens) {
+        const Q4Weight q4w = {weight, scales, biases, y, out_dim};
+        return cuda_status(launch_q4_gemv(x, tokens, &q4w, 1, in_dim, static_cast<cudaStream_t>(stream)));
+    }
     const int np = q4_token_tile(tokens);
     CUtensorMap tx, tw;
     if ((st = tiled_map_2d(x, 2, in_dim, tokens, 64, np, true, &tx)) != PGC_OK) return st;
     if ((st = tiled_map_2d(weight, 4, in_dim / 8, out_dim, 32, 128, true, &tw)) != PGC_OK) return st;
     return cuda_status(launch_q4_linear(tx, tw, tokens, scales, biases, y, out_dim, in_dim,
                                         static_cast<cudaStream_t>(stream)));
+}
+
+int pgc_q4_linear_multi(const uint16_t *x, int tokens, int in_dim, int n_weights,
+                        const uint32_t *const *weights, const uint16_t *const *scales,
+                        const uint16_t *const *biases, uint16_t *const *outs, const int *out_dims,
+                        void *stream) {
+    int st = check_device(nullptr);
+    if (st != PGC_OK) return st;
+    if (n_weights < 1 || n_weights > PGC_LINEAR_MAX_WEIGHTS || !weights || !scales || !biases || !outs ||
+        !out_dims)
+        return PGC_ERR_INVALID;
+    if (tokens > kQ4GemvMaxTokens) {
+        // the tensor-core projection: one launch per weight, each a pass over its packed words
+        for (int i = 0; i < n_weights; ++i)
+            if ((st = pgc_q4_linear(x, tokens, weights[i], scales[i], biases[i], outs[i], out_dims[i], in_dim,
+                                    stream)) != PGC_OK)
+                return st;
+        return PGC_OK;
+    }
+    if (tokens < 0 || in_dim <= 0 || in_dim % 2048 != 0 || in_dim > 8192) return PGC_ERR_INVALID;
+    Q4Weight q4w[PGC_LINEAR_MAX_WEIGHTS];
+    for (int i = 0; i < n_weights; ++i) {
+        if (out_dims[i] <= 0 || out_dims[i] % 64 != 0) return PGC_ERR_INVALID;
+        if (!weights[i] || !scales[i] || !biases[i] || !outs[i]) return PGC_ERR_INVALID;
+        if (!al16(weights[i]) || !al16(scales[i]) || !al16(biases[i]) || ((uintptr_t)outs[i] & 1u) != 0)
+            return PGC_ERR_ALIGN;
+        q4w[i] = {weights[i], scales[i], biases[i], outs[i], out_dims[i]};
+    }
+    if (tokens == 0) return PGC_OK;
+    if (!x) return PGC_ERR_INVALID;
+    if (!al16(x)) return PGC_ERR_ALIGN;
+    return cuda_status(launch_q4_gemv(x, tokens, q4w, n_weights, in_dim, static_cast<cudaStream_t>(stream)));
 }
 
 int pgc_prefill_linear(const uint16_t *x, int tokens, int in_dim, int n_weights,

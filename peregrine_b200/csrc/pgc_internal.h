@@ -141,8 +141,14 @@ cudaError_t launch_q4_linear(const CUtensorMap &tx, const CUtensorMap &tw, int T
 // 1-2 tokens: the CUDA-core stream over the packed words (q4_gemv_kernel); from 3 tokens on
 // the tcgen05 kernel is faster.
 constexpr int kQ4GemvMaxTokens = 2;
-cudaError_t launch_q4_gemv(const uint16_t *x, int T, const uint32_t *w, const uint16_t *scales,
-                           const uint16_t *biases, uint16_t *y, int out_dim, int in_dim, cudaStream_t stream);
+struct Q4Weight {
+    const uint32_t *w;
+    const uint16_t *scales, *biases;
+    uint16_t *y;
+    int out_dim;
+};
+// n (<= PGC_LINEAR_MAX_WEIGHTS) weights that share x, one launch
+cudaError_t launch_q4_gemv(const uint16_t *x, int T, const Q4Weight *ws, int n, int in_dim, cudaStream_t stream);
 cudaError_t q4_read_error(DevErrorHost *e, bool clear);
 
 // prefill_linear.cu

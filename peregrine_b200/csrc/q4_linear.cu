@@ -86,17 +86,40 @@ constexpr int kGemvRows = 4;  // output rows per warp
 __device__ __forceinline__ float q128_f32(uint32_t nibbles, int k) {
     return __uint_as_float(__byte_perm(nibbles, 0x43000000u, 0x7054u | (k << 8)));
 }
+// Up to PGC_LINEAR_MAX_WEIGHTS weights that share the input (the q | gate, k and v projections)
+// run as one launch: their 32-row CTA blocks form one grid.
+struct Q4GemvGroups {
+    const uint32_t *w[PGC_LINEAR_MAX_WEIGHTS];
+    const uint16_t *scales[PGC_LINEAR_MAX_WEIGHTS];
+    const uint16_t *biases[PGC_LINEAR_MAX_WEIGHTS];
+    uint16_t *y[PGC_LINEAR_MAX_WEIGHTS];
+    int out_dim[PGC_LINEAR_MAX_WEIGHTS];
+    int block_begin[PGC_LINEAR_MAX_WEIGHTS];  // first CTA of each weight
+    int n;
+};
+
 template <int T>
-__global__ void __launch_bounds__(256) q4_gemv_kernel(const uint16_t *x, const uint32_t *w,
-                                                      const uint16_t *scales, const uint16_t *biases,
-                                                      uint16_t *y, int out_dim, int in_dim) {
+__global__ void __launch_bounds__(256) q4_gemv_kernel(const uint16_t *x, const Q4GemvGroups gp, int in_dim) {
     pdl_trigger();
     pdl_wait();
+    // this CTA's weight (constant parameter indices only: a dynamically indexed parameter array
+    // would be copied to local memory)
+    const int b = blockIdx.x;
+    const int gi = (gp.n > 1 && b >= gp.block_begin[1]) + (gp.n > 2 && b >= gp.block_begin[2]) +
+                   (gp.n > 3 && b >= gp.block_begin[3]);
+#define Q4_PICK(field) (gi == 0 ? gp.field[0] : gi == 1 ? gp.field[1] : gi == 2 ? gp.field[2] : gp.field[3])
+    const uint32_t *w = Q4_PICK(w);
+    const uint16_t *scales = Q4_PICK(scales);
+    const uint16_t *biases = Q4_PICK(biases);
+    uint16_t *y = Q4_PICK(y);
+    const int out_dim = Q4_PICK(out_dim);
+    const int block0 = Q4_PICK(block_begin);
+#undef Q4_PICK
     // shared memory: x [T][in_dim] bf16, then this CTA's 32 rows of scales and of biases
     // ([32][groups] each, one contiguous block of the [out][groups] arrays)
     extern __shared__ __align__(16) uint16_t gx[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int rc = blockIdx.x * 8 * kGemvRows;  // first row of the CTA
+    const int rc = (b - block0) * 8 * kGemvRows;  // first row of the CTA within its weight
     const int r0 = rc + warp * kGemvRows;
     const int words = in_dim / 8, groups = in_dim / kQ4Group;
     const int runs = words / 128;
@@ -653,7 +676,7 @@ static cudaError_t launch_q4_tc(const CUtensorMap &tx, const CUtensorMap &tw, in
     const int row_tiles = (out_dim + 127) / 128, tok_tiles = (T + NP - 1) / NP;
     const int S = q4_splits(row_tiles * tok_tiles, groups, sms, C::kMaxG);
     const int bytes = C::bytes(groups / S);
-    static int attr_bytes[64] = {};
+    static std::atomic<int> attr_bytes[64] = {};
     if (dev < 0 || dev >= 64 || attr_bytes[dev] < bytes) {
         cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
         if (e != cudaSuccess) return e;
@@ -690,15 +713,26 @@ cudaError_t launch_q4_linear(const CUtensorMap &tx, const CUtensorMap &tw, int T
     }
 }
 
-cudaError_t launch_q4_gemv(const uint16_t *x, int T, const uint32_t *w, const uint16_t *scales,
-                           const uint16_t *biases, uint16_t *y, int out_dim, int in_dim, cudaStream_t stream) {
-    const dim3 grid((unsigned)((out_dim + 8 * kGemvRows - 1) / (8 * kGemvRows)));
+cudaError_t launch_q4_gemv(const uint16_t *x, int T, const Q4Weight *ws, int n, int in_dim, cudaStream_t stream) {
+    if (T < 1 || T > kQ4GemvMaxTokens || n < 1 || n > PGC_LINEAR_MAX_WEIGHTS) return cudaErrorInvalidValue;
+    Q4GemvGroups gp = {};
+    int blocks = 0;
+    for (int i = 0; i < n; ++i) {
+        gp.w[i] = ws[i].w;
+        gp.scales[i] = ws[i].scales;
+        gp.biases[i] = ws[i].biases;
+        gp.y[i] = ws[i].y;
+        gp.out_dim[i] = ws[i].out_dim;
+        gp.block_begin[i] = blocks;
+        blocks += (ws[i].out_dim + 8 * kGemvRows - 1) / (8 * kGemvRows);
+    }
+    gp.n = n;
+    const dim3 grid((unsigned)blocks);
     const size_t smem = ((size_t)T * in_dim + 2 * 8 * kGemvRows * (in_dim / kQ4Group)) * 2;
     static std::atomic<bool> attr_set[64][kQ4GemvMaxTokens] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     auto go = [&](auto kernel) {
-        if (T < 1 || T > kQ4GemvMaxTokens) return cudaErrorInvalidValue;
         if (dev < 0 || dev >= 64 || !attr_set[dev][T - 1]) {
             // largest: T tokens of 8192 inputs + 2 x 32 rows of 128 groups
             cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -706,7 +740,7 @@ cudaError_t launch_q4_gemv(const uint16_t *x, int T, const uint32_t *w, const ui
             if (e != cudaSuccess) return e;
             if (dev >= 0 && dev < 64) attr_set[dev][T - 1] = true;
         }
-        return launch_pdl(kernel, grid, dim3(256), smem, stream, x, w, scales, biases, y, out_dim, in_dim);
+        return launch_pdl(kernel, grid, dim3(256), smem, stream, x, gp, in_dim);
     };
     switch (T) {
         case 1: return go(q4_gemv_kernel<1>);

@@ -78,3 +78,36 @@ def test_q4_linear_matches_oracle(cuda, oracle, out_dim, T, in_dim):
     tol = np.abs(ref) * 2 ** -7 + 1e-3 * np.sqrt((ref ** 2).mean())
     bad = np.abs(got - ref) > tol
     assert not bad.any(), f"{bad.sum()} of {bad.size} beyond tolerance, max {np.abs(got - ref).max():.3e}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [1, 2, 5, 64])
+def test_q4_linear_multi_matches_single(cuda, oracle, T):
+    """pgc_q4_linear_multi over the decode step's weights that share x (q | gate 8192, k 1024,
+    v 1024): at 1-2 tokens one grouped GEMV launch, beyond that one tensor-core pass per
+    weight; each output bit-identical to pgc_q4_linear on that weight alone and within the
+    projection tolerance of the oracle."""
+    import torch
+    in_dim = 4096
+    outs = [8192, 1024, 1024]
+    ws = [_weights(oracle, o, in_dim, 30 + i) for i, o in enumerate(outs)]
+    x = oracle.normal_bf16(T * in_dim, 40 + T).reshape(T, in_dim)
+
+    def dv(a, dt):
+        return torch.from_numpy(a.view(dt)).cuda()
+
+    xd = dv(x, np.int16)
+    wd = [(dv(w, np.int32), dv(sc, np.int16), dv(bi, np.int16)) for w, sc, bi in ws]
+    multi = [torch.empty((T, o), dtype=torch.int16, device="cuda") for o in outs]
+    cuda.q4_linear_multi(xd, [a for a, _, _ in wd], [b for _, b, _ in wd], [c for _, _, c in wd], multi)
+    single = [torch.empty((T, o), dtype=torch.int16, device="cuda") for o in outs]
+    for (a, b, c), y in zip(wd, single):
+        cuda.q4_linear(xd, a, b, c, y)
+    torch.cuda.synchronize()
+    for i, (m, s1) in enumerate(zip(multi, single)):
+        assert torch.equal(m, s1), i
+    w0, sc0, bi0 = ws[1]
+    got = oracle.bf16_to_f32(multi[1].cpu().numpy().view(np.uint16))
+    ref = oracle.bf16_to_f32(oracle.q4_linear(x, w0, sc0, bi0))
+    tol = np.abs(ref) * 2 ** -7 + 1e-3 * np.sqrt((ref ** 2).mean())
+    assert not (np.abs(got - ref) > tol).any()
