@@ -71,16 +71,19 @@ __global__ void __launch_bounds__(256) q4_dequant_kernel(const uint32_t *w, cons
 
 // Decode projection for 1-2 tokens (the reference's single-sequence GEMV,
 // linear_q4_affine_group64_qmv_fast_bf16, linear.metal:64-123) on the CUDA cores: at this batch
-// a weight feeds T FMAs, so the kernel is a stream of packed words. Each warp owns 4 output
-// rows; lane l takes words 4l..4l+3 of every 128-word run of a row (16 bytes, half a group),
-// so a warp reads 512 contiguous bytes per row and run, and issues the loads of 4 runs (16 per
-// lane at one token) before any arithmetic. x and the CTA's scales and biases are copied to
-// shared memory once per CTA; x serves the 4 rows of every warp. Per half
+// a weight feeds T FMAs, so the kernel is a stream of packed words. Each warp owns 2 (one
+// token) or 4 (two tokens) output rows; lane l takes words 4l..4l+3 of every 128-word run of a
+// row (16 bytes, half a group), so a warp reads 512 contiguous bytes per row and run, and
+// issues the loads of 4 runs before any arithmetic. x and the CTA's scales and biases are
+// copied to shared memory once per CTA; x serves the rows of every warp. Per half
 // group the lane accumulates sum((128 + q) x) (each nibble as the float 128 + q, exact) and
 // sum(x), then adds scale * that + (bias - 128 scale) * sum(x); the lanes' sums meet in a
 // butterfly at the end. Each nibble becomes the float 128 + q with one byte permute, and the
 // products run as paired fp32 FMAs, so a weight costs about two issue slots at one token.
-constexpr int kGemvRows = 4;  // output rows per warp
+// Output rows per warp: 2 at one token (more warps in flight: the 8-layer step 0.156 -> 0.134 ms),
+// 4 at two tokens (each weight word then feeds more FMAs).
+template <int T>
+constexpr int gemv_rows() { return T == 1 ? 2 : 4; }
 // Byte k of `nibbles` (a nibble in its low 4 bits) as the float 128 + q: the byte lands in bits
 // 16-23 under the exponent byte 0x43 (2^7), so q sits in the top mantissa bits, worth 1 each.
 __device__ __forceinline__ float q128_f32(uint32_t nibbles, int k) {
@@ -100,6 +103,7 @@ struct Q4GemvGroups {
 
 template <int T>
 __global__ void __launch_bounds__(256) q4_gemv_kernel(const uint16_t *x, const Q4GemvGroups gp, int in_dim) {
+    constexpr int kGemvRows = gemv_rows<T>();
     pdl_trigger();
     pdl_wait();
     // this CTA's weight (constant parameter indices only: a dynamically indexed parameter array
@@ -715,6 +719,7 @@ cudaError_t launch_q4_linear(const CUtensorMap &tx, const CUtensorMap &tw, int T
 
 cudaError_t launch_q4_gemv(const uint16_t *x, int T, const Q4Weight *ws, int n, int in_dim, cudaStream_t stream) {
     if (T < 1 || T > kQ4GemvMaxTokens || n < 1 || n > PGC_LINEAR_MAX_WEIGHTS) return cudaErrorInvalidValue;
+    const int cta_rows = 8 * (T == 1 ? gemv_rows<1>() : gemv_rows<2>());
     Q4GemvGroups gp = {};
     int blocks = 0;
     for (int i = 0; i < n; ++i) {
@@ -724,11 +729,11 @@ cudaError_t launch_q4_gemv(const uint16_t *x, int T, const Q4Weight *ws, int n, 
         gp.y[i] = ws[i].y;
         gp.out_dim[i] = ws[i].out_dim;
         gp.block_begin[i] = blocks;
-        blocks += (ws[i].out_dim + 8 * kGemvRows - 1) / (8 * kGemvRows);
+        blocks += (ws[i].out_dim + cta_rows - 1) / cta_rows;
     }
     gp.n = n;
     const dim3 grid((unsigned)blocks);
-    const size_t smem = ((size_t)T * in_dim + 2 * 8 * kGemvRows * (in_dim / kQ4Group)) * 2;
+    const size_t smem = ((size_t)T * in_dim + 2 * cta_rows * (in_dim / kQ4Group)) * 2;
     static std::atomic<bool> attr_set[64][kQ4GemvMaxTokens] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -736,7 +741,7 @@ cudaError_t launch_q4_gemv(const uint16_t *x, int T, const Q4Weight *ws, int n, 
         if (dev < 0 || dev >= 64 || !attr_set[dev][T - 1]) {
             // largest: T tokens of 8192 inputs + 2 x 32 rows of 128 groups
             cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (T * 8192 + 2 * 8 * kGemvRows * 128) * 2);
+                                                 (T * 8192 + 2 * cta_rows * 128) * 2);
             if (e != cudaSuccess) return e;
             if (dev >= 0 && dev < 64) attr_set[dev][T - 1] = true;
         }
