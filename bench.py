@@ -843,8 +843,10 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
     the ranks in contiguous page-aligned KV shards; per layer: q/k RoPE (the new K/V row lands
     on the rank owning position 262144), split-K decode over the local shard, exchange of the
     (m, l, o) partials and LSE merge + gate on every rank. Timed twice: with the library's
-    peer-memory exchange kernel (the reported figure) and with the library's NCCL path
-    (pgc_cp_decode_attn_nccl: partials, in-place ncclAllGather, merge)."""
+    peer-memory exchange kernel and the append fused into the split kernel
+    (pgc_cp_decode_attn_append, the reported figure), and with the library's NCCL path after a
+    separate append (pgc_append_kv_rope, then pgc_cp_decode_attn_nccl: partials, in-place
+    ncclAllGather, merge)."""
     import torch
     import torch.distributed as dist
     from peregrine_b200 import cp
@@ -881,11 +883,11 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
     grp = cp.NcclGroup(world, rank)
 
     def step_peer():
+        # the append fused into the split kernel (pgc_cp_decode_attn_append): one launch pair
+        # (split + exchange) per layer
         for l in range(layers):
-            capi.append_kv_rope(q_in[l], q, k_in[l], v_in[l], rope, pos, slot, kp[l], vp[l],
-                                gate_out=gate, stream=s)
-            ex.decode_layer(q.view(1, 1, NQ, D), kp[l], vp[l], table, local_len, n, SCALE, ws, out,
-                            gate=gate.view(NQ, D), stream=s)
+            ex.decode_layer_append(q_in[l], k_in[l], v_in[l], rope, pos, slot, s0, kp[l], vp[l], table,
+                                   local_len, n, SCALE, ws, out, stream=s)
 
     def step_nccl():
         for l in range(layers):
@@ -922,10 +924,10 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
     from oracle import oracle
     step_peer()
     torch.cuda.synchronize()
-    out_peer, q_last, g_last = out.clone(), q.clone(), gate.clone()
+    out_peer = out.clone()
     step_nccl()
     torch.cuda.synchronize()
-    out_nccl = out.clone()
+    out_nccl, q_last, g_last = out.clone(), q.clone(), gate.clone()
     code2, _ = capi.device_error()
     diff_paths = (out_peer.float() - out_nccl.float()).abs().max().item()
     if world > 1:
@@ -954,8 +956,9 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
     if world > 1:
         dist.all_reduce(chk, op=dist.ReduceOp.MAX)
     err, bad, diff_paths, ranks_differ, dev_err = chk.tolist()
-    parity = {"check": "last layer: peer-exchange output vs the oracle (per-rank shard partials "
-                       "on the host, gathered, LSE-merged, gated), vs the NCCL path, and across ranks",
+    parity = {"check": "last layer: peer-exchange output (append fused) vs the oracle (per-rank shard "
+                       "partials on the host, gathered, LSE-merged, gated), vs the NCCL path (separate "
+                       "append), and across ranks",
               "tolerance": "abs 2e-2 + rel 1e-2 vs oracle; paths within 1 bf16 ulp",
               "max_abs_err_vs_oracle": err, "bad_elements": int(bad),
               "max_abs_diff_peer_vs_nccl": diff_paths, "ranks_identical": ranks_differ == 0,

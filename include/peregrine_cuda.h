@@ -557,6 +557,22 @@ int pgc_cp_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_
                        uint16_t *out, void *workspace, size_t workspace_bytes,
                        void *const *buffers, int world, int rank, uint32_t epoch, void *stream);
 
+/* pgc_cp_decode_attn with the decode append of the step fused in, as pgc_decode_attn_append does
+ * for one GPU: every rank computes the query rows (RMSNorm + RoPE at the global `position`) from
+ * the packed q | gate input (q_head_stride 512; 256 for q alone, ungated), and the rank whose
+ * shard holds the new token writes its K/V rows at `slot` (its index in this rank's pool; -1 on
+ * the other ranks). `shard_start` is the global position of this rank's first cached token, so
+ * position - shard_start is the token's index in the shard (seq_len counts it on the owner).
+ * One token per call; the rest as pgc_cp_decode_attn. */
+int pgc_cp_decode_attn_append(const uint16_t *q_in, int q_head_stride, const uint16_t *k_in,
+                              const uint16_t *v_in, const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                              const float *rope_table, int64_t rope_max_pos, const int32_t *position,
+                              const int64_t *slot, int64_t shard_start, uint16_t *k_pages,
+                              uint16_t *v_pages, int64_t num_pages, const int32_t *block_table, int max_pages,
+                              const int32_t *seq_len, int max_seq_len, float scale, uint16_t *out,
+                              void *workspace, size_t workspace_bytes, void *const *buffers, int world,
+                              int rank, uint32_t epoch, void *stream);
+
 /* The same context-parallel decode with the partials exchanged by an NCCL all-gather (the
  * reference is single device; BASELINE config 5b names this collective). One layer:
  * pgc_decode_attn_partials over the local shard into this rank's slot of `gathered`

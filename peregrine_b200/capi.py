@@ -143,6 +143,8 @@ SIGNATURES = {
     "pgc_nccl_comm_init": (I32, [I32, I32, P, P]),
     "pgc_nccl_comm_destroy": (I32, [P]),
     "pgc_cp_decode_attn_nccl": (I32, [P, P, P, I64, P, I32, P, I32, F32, P, P, P, P, SZ, P, P]),
+    "pgc_cp_decode_attn_append": (I32, [P, I32, P, P, P, P, P, I64, P, P, I64, P, P, I64, P, I32, P, I32, F32,
+                                        P, P, SZ, C.POINTER(P), I32, I32, C.c_uint32, P]),
     "pgc_page_pool_create": (P, [I32]),
     "pgc_page_pool_destroy": (None, [P]),
     "pgc_page_pool_alloc": (I32, [P, I32, P]),

@@ -115,6 +115,25 @@ class PeerExchange:
             self.world, self.rank, self.epoch, capi._stream(stream)), "pgc_cp_decode_attn")
 
 
+    def decode_layer_append(self, q_in, k_in, v_in, rope, position, slot, shard_start, k_pages, v_pages,
+                            block_table, local_len_dev, local_max_len, scale, workspace, out,
+                            q_norm_w=None, k_norm_w=None, stream=None) -> None:
+        """decode_layer with the step's append fused in (pgc_cp_decode_attn_append): q_in is
+        the packed q | gate [1, 16, 512] (or q alone [1, 16, 256]), position [1] the global
+        position (RoPE), slot [1] the new token's index in this rank's pool or -1 where another
+        rank owns it, shard_start this rank's first global position."""
+        self.epoch += 1
+        capi.check(capi.lib().pgc_cp_decode_attn_append(
+            q_in.data_ptr(), q_in.shape[-1], k_in.data_ptr(), v_in.data_ptr(),
+            None if q_norm_w is None else q_norm_w.data_ptr(),
+            None if k_norm_w is None else k_norm_w.data_ptr(), rope.data_ptr(), rope.shape[0],
+            position.data_ptr(), slot.data_ptr(), shard_start, k_pages.data_ptr(), v_pages.data_ptr(),
+            k_pages.shape[0], block_table.data_ptr(), block_table.shape[-1], local_len_dev.data_ptr(),
+            max(local_max_len, 1), scale, out.data_ptr(), workspace.data_ptr(),
+            workspace.numel() * workspace.element_size(), self.buffers, self.world, self.rank, self.epoch,
+            capi._stream(stream)), "pgc_cp_decode_attn_append")
+
+
 class NcclGroup:
     """An NCCL communicator of the context-parallel group, made through the library's C ABI:
     rank 0 draws the unique id (pgc_nccl_get_unique_id), the 128 bytes travel over the process

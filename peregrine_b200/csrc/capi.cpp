@@ -704,6 +704,55 @@ int pgc_cp_decode_attn(const uint16_t *q, const uint16_t *k_pages, const uint16_
                                         v_pages));
 }
 
+int pgc_cp_decode_attn_append(const uint16_t *q_in, int q_head_stride, const uint16_t *k_in,
+                              const uint16_t *v_in, const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                              const float *rope_table, int64_t rope_max_pos, const int32_t *position,
+                              const int64_t *slot, int64_t shard_start, uint16_t *k_pages,
+                              uint16_t *v_pages, int64_t num_pages, const int32_t *block_table, int max_pages,
+                              const int32_t *seq_len, int max_seq_len, float scale, uint16_t *out,
+                              void *workspace, size_t workspace_bytes, void *const *buffers, int world,
+                              int rank, uint32_t epoch, void *stream) {
+    int st = decode_checks(q_in, k_pages, v_pages, num_pages, block_table, max_pages, seq_len, 1, 1,
+                           max_seq_len, workspace, workspace_bytes);
+    if (st != PGC_OK) return st;
+    if (!out || !buffers || !std::isfinite(scale) || !k_in || !v_in || !rope_table || !position || !slot ||
+        rope_max_pos <= 0 || shard_start < 0)
+        return PGC_ERR_INVALID;
+    if (q_head_stride != PGC_HEAD_DIM && q_head_stride != 2 * PGC_HEAD_DIM) return PGC_ERR_INVALID;
+    if (world < 1 || world > PGC_CP_MAX_RANKS || rank < 0 || rank >= world || epoch == 0)
+        return PGC_ERR_INVALID;
+    float *bufs[PGC_CP_MAX_RANKS] = {};
+    for (int i = 0; i < world; ++i) {
+        if (!buffers[i] || !al16(buffers[i])) return PGC_ERR_INVALID;
+        bufs[i] = static_cast<float *>(buffers[i]);
+    }
+    if (!al16(out)) return PGC_ERR_ALIGN;
+    CUtensorMap tk, tv;
+    if ((st = pool_tensor_map(k_pages, num_pages, &tk)) != PGC_OK) return st;
+    if ((st = pool_tensor_map(v_pages, num_pages, &tv)) != PGC_OK) return st;
+    DecodeAppend app;
+    app.q_in = q_in;
+    app.q_head_stride = q_head_stride;
+    app.k_in = k_in;
+    app.v_in = v_in;
+    app.q_norm_w = q_norm_w;
+    app.k_norm_w = k_norm_w;
+    app.rope = rope_table;
+    app.rope_max_pos = rope_max_pos;
+    app.positions = position;
+    app.slots = slot;
+    app.k_pages = k_pages;
+    app.v_pages = v_pages;
+    app.num_pages = num_pages;
+    app.pos_offset = shard_start;
+    // packed q | gate rows: the gate is the second half of each 512-wide head row
+    const uint16_t *gate = q_head_stride == 2 * PGC_HEAD_DIM ? q_in + PGC_HEAD_DIM : nullptr;
+    return cuda_status(launch_cp_decode(nullptr, tk, tv, num_pages, block_table, max_pages, seq_len, max_seq_len,
+                                        scale, gate, out, workspace, bufs, world, rank, epoch,
+                                        current_sm_count(), static_cast<cudaStream_t>(stream), k_pages,
+                                        v_pages, &app, q_head_stride));
+}
+
 // ------------------------------------------------------------------ q4 projections
 int pgc_q4_dequantize(const uint32_t *weight, const uint16_t *scales, const uint16_t *biases,
                       uint16_t *out, int out_dim, int in_dim, void *stream) {

@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             int32_t newpos[PGC_MAX_QUERIES];
 #pragma unroll
             for (int j = 0; j < PGC_MAX_QUERIES; ++j)
-                newpos[j] = (kFused && j < nq) ? p.app.positions[(int64_t)seq * nq + j] : -1;
+                newpos[j] = (kFused && j < nq) ? (int32_t)(p.app.positions[(int64_t)seq * nq + j] - p.app.pos_offset) : -1;
             const int32_t *table =
                 p.block_tables + (int64_t)seq * p.max_pages_per_seq + split * p.pages_per_split;
             auto prefetch_page = [&](int i) {
@@ -240,13 +240,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int j = 0; j < PGC_MAX_QUERIES; ++j) pos[j] = j < nq ? a.positions[tb + j] : -1;
         const int64_t slot = warp < nq ? a.slots[tb + warp] : -1;
         const int32_t kpos = warp < nq ? a.positions[tb + warp] : -1;  // the K/V token's position
+        // its index in this sequence's cache (a context-parallel shard starts at pos_offset)
+        const int64_t klocal = (int64_t)kpos - a.pos_offset;
         // The appended tokens normally sit at L - nq + j: their RoPE rows are fetched for that
         // guess in the same round as the positions, and fetched again only where a position
         // differs.
         float xq[PGC_MAX_QUERIES][8], cq[PGC_MAX_QUERIES], sq[PGC_MAX_QUERIES], qwf[8];
 #pragma unroll
         for (int j = 0; j < PGC_MAX_QUERIES; ++j) {
-            const int32_t guess = L - nq + j;
+            const int32_t guess = (int32_t)(L - nq + j + a.pos_offset);
             const bool gok = j < nq && guess >= 0 && guess < a.rope_max_pos;
             cq[j] = gok ? a.rope[(int64_t)guess * kRot + lane] : 0.f;
             sq[j] = gok ? a.rope[(int64_t)guess * kRot + 32 + lane] : 0.f;
@@ -257,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int j = 0; j < PGC_MAX_QUERIES; ++j) {
             const bool ok = j < nq && pos[j] >= 0 && pos[j] < a.rope_max_pos;
-            if (ok && pos[j] != L - nq + j) {
+            if (ok && pos[j] != (int32_t)(L - nq + j + a.pos_offset)) {
                 cq[j] = a.rope[(int64_t)pos[j] * kRot + lane];
                 sq[j] = a.rope[(int64_t)pos[j] * kRot + 32 + lane];
             }
@@ -267,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // the K/V token's rows and its RoPE row (for the guessed position) in the same round
         float xk[8], kwf[8], ck = 0.f, sk = 0.f;
         uint16_t vv[8];
-        const int32_t kguess = L - nq + warp;
+        const int32_t kguess = (int32_t)(L - nq + warp + a.pos_offset);
         if (warp < nq) {
             const int64_t t = tb + warp;
             const uint16_t *ks = a.k_in + (t * kNumKvHeads + kvh) * kHeadDim;
@@ -309,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (warp < nq) {
             if (kv_ok && !page_ok) {
                 if (lane == 0 && kvh == 0 && split == 0) record_error(&g_decode_err, kErrSlotOutOfRange, slot);
-            } else if (page_ok && ((kpos >= tok_begin && kpos < tok_end) || (split == 0 && kpos >= L))) {
+            } else if (page_ok && ((klocal >= tok_begin && klocal < tok_end) || (split == 0 && klocal >= L))) {
                 uint16_t ko[8];
                 append_row_compute(xk, a.k_norm_w != nullptr ? kwf : nullptr, ck, sk, true, ko);
                 const int64_t off = (((slot / kPage) * kNumKvHeads + kvh) * kPage + slot % kPage) * kHeadDim;
@@ -837,6 +839,7 @@ struct CpParams {
     int world, rank;
     uint32_t epoch;
     const uint16_t *gate;
+    int64_t gate_stride;  // elements between gate rows
     uint16_t *out;
 };
 
@@ -930,7 +933,7 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
             const float d2 = (ma == -INFINITY) ? 0.f : sden;
             float v = (d2 == 0.f) ? 0.f : ((ma == -INFINITY) ? 0.f : sacc) / d2;
             if (p.gate) {
-                const float g = bf16_bits_to_f32(p.gate[r * kHeadDim + dd]);
+                const float g = bf16_bits_to_f32(p.gate[r * p.gate_stride + dd]);
                 v = v * (1.0f / (1.0f + expf(-g)));
             }
             p.out[r * kHeadDim + dd] = f32_to_bf16_bits(v);
@@ -992,7 +995,7 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
         const int dd = d0 + lane;
         float v = (d2 == 0.f) ? 0.f : a2 / d2;
         if (p.gate) {
-            const float g = bf16_bits_to_f32(p.gate[r * kHeadDim + dd]);
+            const float g = bf16_bits_to_f32(p.gate[r * p.gate_stride + dd]);
             v = v * (1.0f / (1.0f + expf(-g)));
         }
         p.out[r * kHeadDim + dd] = f32_to_bf16_bits(v);
@@ -1006,19 +1009,23 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
                              const int32_t *seq_len, int max_seq_len, float scale, const uint16_t *gate,
                              uint16_t *out, void *workspace, float *const *bufs, int world, int rank,
                              uint32_t epoch, int sm_count, cudaStream_t stream, const void *k_pages,
-                             const void *v_pages) {
+                             const void *v_pages, const DecodeAppend *app, int64_t gate_stride) {
     static std::atomic<bool> attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
         cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_split_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemBytes);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const DecodePlan plan = decode_plan(1, max_seq_len, sm_count);
     SplitParams sp = {};
     sp.q = q;
+    if (app != nullptr) sp.app = *app;
     sp.block_tables = block_table;
     sp.seq_lens = seq_len;
     sp.ws = static_cast<float *>(workspace);
@@ -1033,8 +1040,10 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
     sp.prefetch_ahead = pf ? plan.prefetch_ahead : 0;
     sp.k_base = static_cast<const uint8_t *>(k_pages);
     sp.v_base = static_cast<const uint8_t *>(v_pages);
-    cudaError_t e = launch_pdl(decode_split_kernel<false>, dim3(plan.max_splits, kNumKvHeads, 1), dim3(kThreads),
-                               kSmemBytes, stream, tk, tv, sp);
+    const dim3 grid(plan.max_splits, kNumKvHeads, 1);
+    cudaError_t e = app != nullptr
+                        ? launch_pdl(decode_split_kernel<true>, grid, dim3(kThreads), kSmemBytes, stream, tk, tv, sp)
+                        : launch_pdl(decode_split_kernel<false>, grid, dim3(kThreads), kSmemBytes, stream, tk, tv, sp);
     if (e != cudaSuccess) return e;
     CpParams cp;
     cp.parts = sp.ws;
@@ -1046,6 +1055,7 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
     cp.rank = rank;
     cp.epoch = epoch;
     cp.gate = gate;
+    cp.gate_stride = gate_stride;
     cp.out = out;
     return launch_pdl(cp_exchange_kernel, dim3(kCpRows, kHeadDim / 32), dim3(256), 0, stream, cp);
 }

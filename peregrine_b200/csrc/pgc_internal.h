@@ -51,6 +51,9 @@ struct DecodeAppend {
     const int64_t *slots = nullptr;
     uint16_t *k_pages = nullptr, *v_pages = nullptr;
     int64_t num_pages = 0;
+    // context-parallel shard: positions (RoPE) minus pos_offset give the token's index in this
+    // rank's cache; 0 otherwise
+    int64_t pos_offset = 0;
 };
 cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
                           int64_t num_pages, const int32_t *block_tables, int max_pages_per_seq,
@@ -73,7 +76,8 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
                              const int32_t *seq_len, int max_seq_len, float scale, const uint16_t *gate,
                              uint16_t *out, void *workspace, float *const *bufs, int world, int rank,
                              uint32_t epoch, int sm_count, cudaStream_t stream,
-                             const void *k_pages = nullptr, const void *v_pages = nullptr);
+                             const void *k_pages = nullptr, const void *v_pages = nullptr,
+                             const DecodeAppend *app = nullptr, int64_t gate_stride = 256);
 int decode_static_scratch(void **ptr_out);
 
 // kv_append.cu

@@ -2,7 +2,10 @@
 
 1. world = 1: split decode + exchange kernel over several back-to-back calls (both epoch
    parities) against the oracle over the same cache, within the attention tolerance.
-2. A rank that never arrives: world = 2 where the second rank's buffer is a local stand-in that
+2. The append fused in (pgc_cp_decode_attn_append), world = 1 over a cache whose first global
+   position is not 0, bit for bit against pgc_append_kv_rope followed by pgc_cp_decode_attn
+   (output and pools) over several layers.
+3. A rank that never arrives: world = 2 where the second rank's buffer is a local stand-in that
    nobody publishes to. The exchange kernel's flag wait runs out after its bound (~2 s), the
    library reports PGC_ERR_TIMEOUT's device code through pgc_device_error, and the context stays
    usable: the next world = 1 call is correct. No GPU fault is involved: the wait is bounded and
@@ -104,3 +107,54 @@ def test_peer_exchange_times_out_when_a_rank_never_arrives(cuda, oracle):
     finally:
         for b in (own, absent, solo):
             cuda.lib().pgc_cp_buffer_free(b)
+
+
+def test_fused_append_matches_append_then_exchange(cuda, oracle):
+    """A shard whose first global position is 40000 (so RoPE positions and pool indices differ)
+    with the new token at its end: the fused call and the two calls give the same bits."""
+    import torch
+    from peregrine_b200 import cp
+    L, start = 2500, 40000  # L cached tokens + the new one
+    kp, vp, table = _cache(oracle, L + 1, 8)
+    kp[(L) // PAGE, :, L % PAGE] = 0
+    vp[(L) // PAGE, :, L % PAGE] = 0
+    rope = torch.from_numpy(cuda.rope_table(start + L + 1)).cuda()
+    qw = dev(oracle.normal_bf16(D, 9))
+    kw = dev(oracle.normal_bf16(D, 10))
+    pos = torch.tensor([start + L], dtype=torch.int32, device="cuda")
+    slot = torch.tensor([L], dtype=torch.int64, device="cuda")
+    seq = torch.tensor([L + 1], dtype=torch.int32, device="cuda")
+    ws = torch.empty(cuda.decode_workspace_bytes(1, 1, L + 1), dtype=torch.uint8, device="cuda")
+    outs = {}
+    pools = {}
+    for mode in ("fused", "two_calls"):
+        kd, vd, td = dev(kp), dev(vp), dev(table)
+        ex = cp.PeerExchange(1, 0)
+        res = []
+        try:
+            for layer in range(3):
+                q_in = dev(oracle.normal_bf16(NQ * 2 * D, 20 + layer).reshape(1, NQ, 2 * D))
+                k_in = dev(oracle.normal_bf16(NKV * D, 30 + layer).reshape(1, NKV, D))
+                v_in = dev(oracle.normal_bf16(NKV * D, 40 + layer).reshape(1, NKV, D))
+                out = torch.empty((NQ, D), dtype=torch.int16, device="cuda")
+                if mode == "fused":
+                    ex.decode_layer_append(q_in, k_in, v_in, rope, pos, slot, start, kd, vd, td, seq, L + 1,
+                                           1 / 16, ws, out, q_norm_w=qw, k_norm_w=kw)
+                else:
+                    q = torch.empty((1, NQ, D), dtype=torch.int16, device="cuda")
+                    gate = torch.empty((1, NQ, D), dtype=torch.int16, device="cuda")
+                    cuda.append_kv_rope(q_in, q, k_in, v_in, rope, pos, slot, kd, vd, gate_out=gate,
+                                        q_norm_w=qw, k_norm_w=kw)
+                    ex.decode_layer(q.view(1, 1, NQ, D), kd, vd, td, seq, L + 1, 1 / 16, ws, out,
+                                    gate=gate.view(NQ, D))
+                torch.cuda.synchronize()
+                res.append(out.clone())
+        finally:
+            ex.close()
+        outs[mode] = res
+        pools[mode] = (kd.clone(), vd.clone())
+    for a, b in zip(outs["fused"], outs["two_calls"]):
+        assert torch.equal(a, b)
+    assert torch.equal(pools["fused"][0], pools["two_calls"][0])
+    assert torch.equal(pools["fused"][1], pools["two_calls"][1])
+    assert cuda.device_error() == (0, 0)
