@@ -913,9 +913,17 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def step_local():
+        # this rank's shard decoded alone (split + merge launches, no append, no exchange): the
+        # single-sequence part of a context-parallel layer
+        for l in range(layers):
+            capi.decode_attn(q.view(1, 1, NQ, D), kp[l], vp[l], table, local_len, n, SCALE, out, ws,
+                             gate=gate.view(NQ, D), stream=s)
+
     ms = timed(step_peer)
     code, _ = capi.device_error()
     ms_nccl = timed(step_nccl)
+    ms_local = timed(step_local)
     # Output check (last layer of one more step of each path): the peer-exchange output against
     # the NCCL path's, against every other rank's, and against the oracle, which decodes each
     # rank's shard on the host into (m, l, o) partials that are gathered and LSE-merged with the
@@ -975,7 +983,15 @@ def bench_config5b(capi, rank, world, iters=20, warmup=3):
                         f"pgc_cp_decode_attn_nccl, timed beside it)",
             "ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1),
             "GB_s_aggregate": round(kv / (ms * 1e-3) / 1e9, 1), "kv_bytes": kv,
-            "ms_per_token_nccl": round(ms_nccl, 4), "device_error": code, "parity": parity}
+            "ms_per_token_nccl": round(ms_nccl, 4), "device_error": code,
+            "per_layer_us": {"cp_peer_fused": round(ms * 1e3 / layers, 2),
+                             "cp_nccl": round(ms_nccl * 1e3 / layers, 2),
+                             "local_shard_decode": round(ms_local * 1e3 / layers, 2),
+                             "shard_hbm_floor": round(n * KV_BYTES_PER_TOKEN / (measured_peaks()[0] * 1e9) * 1e6, 2),
+                             "note": "local_shard_decode: the slowest rank's shard through pgc_decode_attn "
+                                     "alone (split + merge, no append, no exchange); cp_peer_fused minus it "
+                                     "is the append and the exchange"},
+            "parity": parity}
 
 
 # ------------------------------------------------------------------------------ GPU arm

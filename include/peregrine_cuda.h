@@ -533,15 +533,15 @@ int pgc_gated_delta_prefill(float *state, int has_previous_state, const uint16_t
  * device). Rank g of `world` (<= PGC_CP_MAX_RANKS) GPUs holds a contiguous KV shard of one
  * sequence. pgc_cp_decode_attn runs the split decode over the local shard and then one exchange
  * kernel that merges the splits, stores the rank's (m, l, o) partial into every rank's exchange
- * buffer, counts its arrival there (a release add on the counter of its source rank), waits
- * (bounded, ~2 s, then PGC_ERR_TIMEOUT through pgc_device_error) until every rank has counted in
- * for this call, and merges the world partials (+ sigmoid gate) into the bf16 output on every
- * rank. No collective library is involved.
+ * buffer as 8-byte words tagged with the call's epoch, polls its own buffer (bounded, ~2 s, then
+ * PGC_ERR_TIMEOUT through pgc_device_error) until every rank's words for this call have landed,
+ * and merges the world partials (+ sigmoid gate) into the bf16 output on every rank. No
+ * collective library and no fence is involved.
  * Setup: each rank allocates its buffer with pgc_cp_buffer_alloc, exports it with
  * pgc_ipc_get_handle, the handles are exchanged by the caller (any host channel) and opened
  * with pgc_ipc_open_handle; `buffers[i]` is rank i's buffer as mapped in this process (its own
  * at [rank]). `epoch` starts at 1 on freshly allocated (zeroed) buffers and increases by one per
- * call, identically on every rank.
+ * call, identically on every rank (2^32 - 1 calls per allocation).
  * ------------------------------------------------------------------------------------- */
 #define PGC_CP_MAX_RANKS 8
 #define PGC_IPC_HANDLE_BYTES 64

@@ -816,18 +816,20 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
 // ------------------------------------------------------------------------------------------
 // Context-parallel exchange over peer memory (BASELINE config 5b). Rank g holds one contiguous
 // KV shard of a long sequence; the split kernel leaves its per-split partials in the
-// workspace. The exchange kernel (one CTA per row and 32-dim chunk) then (1) LSE-merges those splits into the
-// rank's partial (16 rows x (m, l, o[256])), (2) stores it straight into every rank's exchange
-// buffer over NVLink, (3) counts its arrival in each rank's buffer (a release add at system
-// scope on the counter of its source rank), (4) waits until every source rank's counter in its
-// own buffer has counted all 128 CTAs of this call (acquire, bounded) and (5) merges the world
-// partials with the gate into the bf16 output. This replaces merge kernel + all-gather + merge
-// kernel: launched right behind the split kernel (programmatic dependent launch), it is resident
-// when the last split finishes. Exchange buffer per rank: [2 parities][world][16][258] f32, then
-// world u64 arrival counters at cp_flags_offset. The counters only grow (call e is complete
-// from every source at e * 128), so they need no reset; the buffer starts zeroed. Parity
-// epoch & 1 double-buffers the slots: rank r cannot start call e + 2 before every rank has
-// counted in for e + 1, which each does only after finishing its reads of call e.
+// workspace. The exchange kernel (one CTA per row and 32-dim chunk) then (1) LSE-merges those
+// splits into the rank's partial slice (m, l, o[32 dims]), (2) stores the slice straight into
+// every rank's exchange buffer over NVLink as 8-byte words that carry the value in the low half
+// and the call's epoch in the high half, (3) polls its own buffer until every source rank's
+// words of this slice carry the epoch (bounded) and (4) merges the world partials with the gate
+// into the bf16 output. A 64-bit store is single-copy atomic, so a word whose flag is current
+// holds the current value: no fence and no arrival counter sit between the stores and the
+// reads (a system-scope fence after the remote stores cost 7-14 us per call). This replaces
+// merge kernel + all-gather + merge kernel: launched right behind the split kernel
+// (programmatic dependent launch), it is resident when the last split finishes.
+// Exchange buffer per rank: [2 parities][world sources][16 rows][8 chunks][34 words] u64
+// (o[32], m, l). It starts zeroed and epochs start at 1, so no stale word matches. Parity
+// epoch & 1 double-buffers the records: rank r cannot start call e + 2 before every rank has
+// sent it call e + 1, which each does only after finishing its reads of call e.
 constexpr int kCpRows = kNumQHeads;
 
 struct CpParams {
@@ -843,17 +845,25 @@ struct CpParams {
     uint16_t *out;
 };
 
-__device__ __forceinline__ unsigned long long *cp_counters(float *buf, int world) {
-    return reinterpret_cast<unsigned long long *>(reinterpret_cast<uint8_t *>(buf) + cp_flags_offset(world));
+constexpr int kCpWords = 34;  // one record: o[32], m, l
+
+__device__ __forceinline__ int64_t cp_record(int parity, int world, int src, int row, int chunk) {
+    return ((((int64_t)parity * world + src) * kCpRows + row) * (kHeadDim / 32) + chunk) * kCpWords;
+}
+__device__ __forceinline__ void cp_store_word(unsigned long long *a, float v, uint32_t epoch) {
+    const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long cp_load_word(const unsigned long long *a) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
 }
 
 // One CTA per (row, 32-dim chunk), 128 CTAs: the 8 warps stride over the local splits (lane =
 // dim), as the merge kernel does, so the L2 reads of up to 256 split partials per row overlap.
-// Warp w stores the CTA's slice of the row partial (chunk 0 also m and l) into rank w's buffer
-// over NVLink, fences at system scope and adds one to rank w's counter for this source rank.
-// Every CTA then waits for all ranks' counters and merges its slice over the world partials.
-constexpr int kCpCtas = kCpRows * (kHeadDim / 32);
-
+// Warp w stores the CTA's record (o slice, m, l) into rank w's buffer over NVLink; warp 0 then
+// polls the records of every source rank in this rank's buffer and merges them.
 __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
     pdl_trigger();
     pdl_wait();
@@ -940,57 +950,65 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
         }
         return;
     }
-    // this CTA's slice of the rank partial -> every rank's slot [parity][rank][r], then one
-    // arrival on that rank's counter for this source rank
-    const int parity = (int)(p.epoch & 1u);
+    // this CTA's record of the rank partial -> [parity][rank][r][chunk] of every rank's buffer
+    const uint32_t epoch = p.epoch;
+    const int parity = (int)(epoch & 1u);
+    const int chunk = blockIdx.y;
     if (warp < p.world) {
-        float *dst = p.bufs[warp] + (((int64_t)parity * p.world + p.rank) * kCpRows + r) * kPartial;
-        float sacc = 0.f;
+        float sacc = 0.f, sden = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) sacc += wacc[w][lane];
-        dst[2 + d0 + lane] = sacc;
-        if (blockIdx.y == 0 && lane == 0) {
-            float sden = 0.f;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) sden += wden[w];
-            dst[0] = ma;
-            dst[1] = sden;
+        for (int w = 0; w < 8; ++w) {
+            sacc += wacc[w][lane];
+            sden += wden[w];
         }
-        __threadfence_system();
-        __syncwarp();
-        if (lane == 0) {
-            unsigned long long *ctr = cp_counters(p.bufs[warp], p.world) + p.rank;
-            asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(ctr), "l"(1ull) : "memory");
-        }
+        unsigned long long *dst = reinterpret_cast<unsigned long long *>(p.bufs[warp]) +
+                                  cp_record(parity, p.world, p.rank, r, chunk);
+        cp_store_word(dst + lane, sacc, epoch);
+        if (lane == 0) cp_store_word(dst + 32, ma, epoch);
+        if (lane == 1) cp_store_word(dst + 33, sden, epoch);
     }
-    if (tid < p.world) {
-        const unsigned long long *ctr = cp_counters(p.bufs[p.rank], p.world) + tid;
-        const unsigned long long target = (unsigned long long)p.epoch * kCpCtas;
-        const uint64_t t0 = global_timer_ns();
-        for (uint32_t it = 0;; ++it) {
-            unsigned long long v;
-            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ctr) : "memory");
-            if (v >= target) break;
-            if ((it & 63u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
-                record_error(&g_decode_err, kErrWaitTimeout, 1000 + tid);
-                break;
-            }
-        }
-    }
-    __syncthreads();
     if (warp == 0) {
-        // merge this slice over the world partials [parity][src][r] of this rank's buffer
-        const float *mine = p.bufs[p.rank] + ((int64_t)parity * p.world * kCpRows + r) * kPartial;
-        const int64_t stride = (int64_t)kCpRows * kPartial;
+        // every source's record of this slice, once its words carry this epoch; then the merge
+        const unsigned long long *mine = reinterpret_cast<const unsigned long long *>(p.bufs[p.rank]);
+        float mv[PGC_CP_MAX_RANKS], lv[PGC_CP_MAX_RANKS], ov[PGC_CP_MAX_RANKS];
+        const uint64_t t0 = global_timer_ns();
+        bool timed_out = false;
+#pragma unroll
+        for (int c = 0; c < PGC_CP_MAX_RANKS; ++c) {
+            mv[c] = -INFINITY;
+            lv[c] = ov[c] = 0.f;
+            if (c >= p.world) continue;
+            const unsigned long long *rec = mine + cp_record(parity, p.world, c, r, chunk);
+            unsigned long long wo, wm, wl;
+            for (uint32_t it = 0;; ++it) {
+                wo = cp_load_word(rec + lane);
+                wm = cp_load_word(rec + 32);
+                wl = cp_load_word(rec + 33);
+                const bool ready = (uint32_t)(wo >> 32) == epoch && (uint32_t)(wm >> 32) == epoch &&
+                                   (uint32_t)(wl >> 32) == epoch;
+                if (__all_sync(0xffffffffu, ready)) break;
+                if (timed_out) break;
+                if ((it & 63u) == 0) {
+                    // lane 0's clock decides, so the warp leaves the loop together
+                    const bool late = __shfl_sync(0xffffffffu, global_timer_ns() - t0 > 2000000000ull, 0);
+                    if (late) {
+                        if (lane == 0) record_error(&g_decode_err, kErrWaitTimeout, 1000 + c);
+                        timed_out = true;  // the other sources are read once more, then left
+                    }
+                }
+            }
+            mv[c] = __uint_as_float((uint32_t)wm);
+            lv[c] = __uint_as_float((uint32_t)wl);
+            ov[c] = __uint_as_float((uint32_t)wo);
+        }
         float m2 = -INFINITY;
-        for (int c = 0; c < p.world; ++c) m2 = fmaxf(m2, mine[c * stride]);
+        for (int c = 0; c < p.world; ++c) m2 = fmaxf(m2, mv[c]);
         float d2 = 0.f, a2 = 0.f;
         for (int c = 0; c < p.world; ++c) {
-            const float *pc = mine + c * stride;
-            const float mc = pc[0];
+            const float mc = mv[c];
             const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - m2) * kLog2e);
-            d2 += pc[1] * w;
-            a2 += pc[2 + d0 + lane] * w;
+            d2 += lv[c] * w;
+            a2 += ov[c] * w;
         }
         const int dd = d0 + lane;
         float v = (d2 == 0.f) ? 0.f : a2 / d2;
@@ -1002,7 +1020,9 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
     }
 }
 
-size_t cp_buffer_bytes(int world) { return cp_flags_offset(world) + 256; }
+size_t cp_buffer_bytes(int world) {
+    return (size_t)2 * world * kCpRows * (kHeadDim / 32) * kCpWords * sizeof(unsigned long long);
+}
 
 cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
                              int64_t num_pages, const int32_t *block_table, int max_pages,

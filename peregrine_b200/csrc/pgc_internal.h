@@ -66,10 +66,7 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
                                   int64_t part_stride, const uint16_t *gate, uint16_t *out,
                                   cudaStream_t stream);
 cudaError_t decode_read_error(DevErrorHost *e, bool clear);
-// context-parallel exchange buffer: [2][world][16][258] f32, flags at this offset
-__host__ __device__ inline size_t cp_flags_offset(int world) {
-    return ((size_t)2 * world * 16 * 258 * sizeof(float) + 255) & ~(size_t)255;
-}
+// context-parallel exchange buffer: [2][world][16][8][34] u64 epoch-tagged words
 size_t cp_buffer_bytes(int world);
 cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUtensorMap &tv,
                              int64_t num_pages, const int32_t *block_table, int max_pages,

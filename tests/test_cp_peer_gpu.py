@@ -94,7 +94,7 @@ def test_peer_exchange_times_out_when_a_rank_never_arrives(cuda, oracle):
         del seq
         waited = time.time() - t0
         code, detail = cuda.device_error(clear=True)
-        assert code == 4 and detail == 1001, (code, detail)  # decode unit, wait timeout, rank 1's flag
+        assert code == 4 and detail == 1001, (code, detail)  # decode unit, wait timeout, rank 1's records
         assert 1.0 < waited < 30.0, waited
         # the context is still usable
         ref, _ = oracle.decode_paged(q, kp, vp, table, np.array([L], np.int32), 1 / 16, 1,
