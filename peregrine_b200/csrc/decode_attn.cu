@@ -967,39 +967,46 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
         if (lane == 0) cp_store_word(dst + 32, ma, epoch);
         if (lane == 1) cp_store_word(dst + 33, sden, epoch);
     }
-    if (warp == 0) {
-        // every source's record of this slice, once its words carry this epoch; then the merge
-        const unsigned long long *mine = reinterpret_cast<const unsigned long long *>(p.bufs[p.rank]);
-        float mv[PGC_CP_MAX_RANKS], lv[PGC_CP_MAX_RANKS], ov[PGC_CP_MAX_RANKS];
+    // Warp c polls source c's record of this slice in this rank's buffer until its words carry
+    // this epoch (bounded), so the world's records are awaited in parallel rather than as one
+    // chain of dependent round trips; warp 0 then merges them from shared memory in source order.
+    __shared__ float xm[PGC_CP_MAX_RANKS], xl[PGC_CP_MAX_RANKS], xo[PGC_CP_MAX_RANKS][32];
+    if (warp < p.world) {
+        const int c = warp;
+        const unsigned long long *rec =
+            reinterpret_cast<const unsigned long long *>(p.bufs[p.rank]) + cp_record(parity, p.world, c, r, chunk);
         const uint64_t t0 = global_timer_ns();
-        bool timed_out = false;
-#pragma unroll
-        for (int c = 0; c < PGC_CP_MAX_RANKS; ++c) {
-            mv[c] = -INFINITY;
-            lv[c] = ov[c] = 0.f;
-            if (c >= p.world) continue;
-            const unsigned long long *rec = mine + cp_record(parity, p.world, c, r, chunk);
-            unsigned long long wo, wm, wl;
-            for (uint32_t it = 0;; ++it) {
-                wo = cp_load_word(rec + lane);
-                wm = cp_load_word(rec + 32);
-                wl = cp_load_word(rec + 33);
-                const bool ready = (uint32_t)(wo >> 32) == epoch && (uint32_t)(wm >> 32) == epoch &&
-                                   (uint32_t)(wl >> 32) == epoch;
-                if (__all_sync(0xffffffffu, ready)) break;
-                if (timed_out) break;
-                if ((it & 63u) == 0) {
-                    // lane 0's clock decides, so the warp leaves the loop together
-                    const bool late = __shfl_sync(0xffffffffu, global_timer_ns() - t0 > 2000000000ull, 0);
-                    if (late) {
-                        if (lane == 0) record_error(&g_decode_err, kErrWaitTimeout, 1000 + c);
-                        timed_out = true;  // the other sources are read once more, then left
-                    }
+        unsigned long long wo, wm, wl;
+        for (uint32_t it = 0;; ++it) {
+            wo = cp_load_word(rec + lane);
+            wm = cp_load_word(rec + 32);
+            wl = cp_load_word(rec + 33);
+            const bool ready = (uint32_t)(wo >> 32) == epoch && (uint32_t)(wm >> 32) == epoch &&
+                               (uint32_t)(wl >> 32) == epoch;
+            if (__all_sync(0xffffffffu, ready)) break;
+            if ((it & 63u) == 0) {
+                // lane 0's clock decides, so the warp leaves the loop together
+                const bool late = __shfl_sync(0xffffffffu, global_timer_ns() - t0 > 2000000000ull, 0);
+                if (late) {
+                    if (lane == 0) record_error(&g_decode_err, kErrWaitTimeout, 1000 + c);
+                    break;
                 }
             }
-            mv[c] = __uint_as_float((uint32_t)wm);
-            lv[c] = __uint_as_float((uint32_t)wl);
-            ov[c] = __uint_as_float((uint32_t)wo);
+        }
+        if (lane == 0) {
+            xm[c] = __uint_as_float((uint32_t)wm);
+            xl[c] = __uint_as_float((uint32_t)wl);
+        }
+        xo[c][lane] = __uint_as_float((uint32_t)wo);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float mv[PGC_CP_MAX_RANKS], lv[PGC_CP_MAX_RANKS], ov[PGC_CP_MAX_RANKS];
+#pragma unroll
+        for (int c = 0; c < PGC_CP_MAX_RANKS; ++c) {
+            mv[c] = c < p.world ? xm[c] : -INFINITY;
+            lv[c] = c < p.world ? xl[c] : 0.f;
+            ov[c] = c < p.world ? xo[c][lane] : 0.f;
         }
         float m2 = -INFINITY;
         for (int c = 0; c < p.world; ++c) m2 = fmaxf(m2, mv[c]);
