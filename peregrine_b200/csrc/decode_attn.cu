@@ -141,7 +141,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     pdl_wait();
     const int L = p.seq_lens[seq];
     const int tok_begin = split * p.pages_per_split * kPage;
-    if (tok_begin >= L) return;  // uniform across the CTA
+    if (tok_begin >= L) {
+        // A split past the sequence end leaves an empty partial (m = -inf, l = 0; its o is never
+        // read), so the merges take every planned split without reading the lengths again.
+        if (threadIdx.x < nrows) {
+            const int j = threadIdx.x / kGroup, g = threadIdx.x % kGroup;
+            const int64_t row = (int64_t)(seq * nq + j) * kNumQHeads + kvh * kGroup + g;
+            float *dst = p.ws + (row * p.max_splits + split) * kPartial;
+            dst[0] = -INFINITY;
+            dst[1] = 0.f;
+        }
+        return;  // uniform across the CTA
+    }
     const int tok_end = min(L, tok_begin + p.pages_per_split * kPage);
     const int n_pages = (tok_end - tok_begin + kPage - 1) / kPage;
     __syncthreads();  // barriers initialised: the producer may start streaming K/V now
@@ -511,17 +522,13 @@ __global__ void __launch_bounds__(kThreads, 2)
 // Log-sum-exp merge of a row's partials (attention_decode.metal:215-243). One CTA per
 // (row, 32-dim chunk): lane = dim, so every partial row read is a coalesced 128-byte run, and
 // the 8 warps take every 8th partial, so the reads of different partials are independent and
-// overlap instead of forming one serial chain. nparts < 0: derive the part count from the
-// sequence length.
+// overlap instead of forming one serial chain. A part with m = -inf (a split past the sequence
+// end) has weight 0 and its o is not read.
 struct MergeParams {
     const float *parts;
     int64_t row_stride;   // floats between rows
     int64_t part_stride;  // floats between parts of a row
     int nparts;
-    int max_parts;        // upper bound of the part count (parts below it are readable)
-    const int32_t *seq_lens;  // used when nparts < 0
-    int rows_per_seq;
-    int tokens_per_split;
     const uint16_t *gate;
     int64_t gate_stride;  // elements between gate rows
     uint16_t *out;      // bf16 output, or
@@ -545,14 +552,10 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
     const float *base = p.parts + row * p.row_stride;
     float ma = -INFINITY;
     float den = 0.f, acc = 0.f;
-    if (p.max_parts <= kMergeWarps * kMergeCached) {
-        // one round of loads after the part count: every (m, l, o[d]) of this warp's parts, then
-        // the maximum, the weights and the sums from registers
-        int np = p.nparts;
-        if (np < 0) {
-            const int L = p.seq_lens[row / p.rows_per_seq];
-            np = (L + p.tokens_per_split - 1) / p.tokens_per_split;
-        }
+    const int np = p.nparts;
+    if (np <= kMergeWarps * kMergeCached) {
+        // one round of loads: every (m, l, o[d]) of this warp's parts, then the maximum, the
+        // weights and the sums from registers
         float mc[kMergeCached], lc[kMergeCached], oc[kMergeCached];
 #pragma unroll
         for (int i = 0; i < kMergeCached; ++i) {
@@ -563,7 +566,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
                 const float *pc = base + c * p.part_stride;
                 mc[i] = pc[0];
                 lc[i] = pc[1];
-                oc[i] = pc[2 + d];
+                oc[i] = pc[2 + d];  // read even for an empty part: it is not summed
             }
         }
 #pragma unroll
@@ -583,11 +586,6 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
             }
         }
     } else {
-        int np = p.nparts;
-        if (np < 0) {
-            const int L = p.seq_lens[row / p.rows_per_seq];
-            np = (L + p.tokens_per_split - 1) / p.tokens_per_split;
-        }
         for (int c = threadIdx.x; c < np; c += kMergeWarps * 32) ma = fmaxf(ma, base[c * p.part_stride]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
@@ -600,7 +598,8 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
         for (int c = warp; c < np; c += kMergeWarps) {
             const float *pc = base + c * p.part_stride;
             const float mcv = pc[0];
-            const float w = (mcv == -INFINITY) ? 0.f : exp2f((mcv - ma) * kLog2e);
+            if (mcv == -INFINITY) continue;
+            const float w = exp2f((mcv - ma) * kLog2e);
             den += pc[1] * w;
             acc += pc[2 + d] * w;
         }
@@ -768,11 +767,7 @@ cudaError_t launch_decode(const uint16_t *q, const CUtensorMap &tk, const CUtens
     mp.parts = sp.ws;
     mp.row_stride = (int64_t)plan.max_splits * kPartial;
     mp.part_stride = kPartial;
-    mp.nparts = -1;
-    mp.max_parts = plan.max_splits;
-    mp.seq_lens = seq_lens;
-    mp.rows_per_seq = num_queries * kNumQHeads;
-    mp.tokens_per_split = plan.pages_per_split * kPage;
+    mp.nparts = plan.max_splits;  // splits past a sequence's end left empty partials
     mp.gate = gate;
     mp.gate_stride = gate_stride;
     mp.out = out;
@@ -790,10 +785,6 @@ cudaError_t launch_merge_partials(const float *partials, int64_t rows, int num_p
     mp.row_stride = kPartial;
     mp.part_stride = part_stride;
     mp.nparts = num_parts;
-    mp.max_parts = num_parts;
-    mp.seq_lens = nullptr;
-    mp.rows_per_seq = 1;
-    mp.tokens_per_split = 1;
     mp.gate = gate;
     mp.gate_stride = kHeadDim;
     mp.out = out;
@@ -835,8 +826,6 @@ constexpr int kCpRows = kNumQHeads;
 struct CpParams {
     const float *parts;  // split partials [16][max_splits][258]
     int max_splits;
-    const int32_t *seq_len;
-    int tokens_per_split;
     float *bufs[PGC_CP_MAX_RANKS];  // every rank's exchange buffer, as mapped in this process
     int world, rank;
     uint32_t epoch;
@@ -870,9 +859,7 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
     __shared__ float wm[8], wden[8], wacc[8][32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r = blockIdx.x, d0 = blockIdx.y * 32;
-    const int L = *p.seq_len;
-    int np = L > 0 ? (L + p.tokens_per_split - 1) / p.tokens_per_split : 0;
-    if (np > p.max_splits) np = p.max_splits;
+    const int np = p.max_splits;  // splits past the shard's end left empty partials
     const float *base = p.parts + (int64_t)r * p.max_splits * kPartial;
     float ma = -INFINITY;
     float den = 0.f, acc = 0.f;
@@ -890,7 +877,7 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
                 const float *pc = base + (int64_t)c * kPartial;
                 mc[i] = pc[0];
                 lc[i] = pc[1];
-                oc[i] = pc[2 + d0 + lane];
+                oc[i] = pc[2 + d0 + lane];  // read even for an empty part: it is not summed
             }
         }
 #pragma unroll
@@ -921,7 +908,8 @@ __global__ void __launch_bounds__(256) cp_exchange_kernel(const CpParams p) {
         for (int c = warp; c < np; c += 8) {
             const float *pc = base + (int64_t)c * kPartial;
             const float mc = pc[0];
-            const float w = (mc == -INFINITY) ? 0.f : exp2f((mc - ma) * kLog2e);
+            if (mc == -INFINITY) continue;
+            const float w = exp2f((mc - ma) * kLog2e);
             den += pc[1] * w;
             acc += pc[2 + d0 + lane] * w;
         }
@@ -1075,8 +1063,6 @@ cudaError_t launch_cp_decode(const uint16_t *q, const CUtensorMap &tk, const CUt
     CpParams cp;
     cp.parts = sp.ws;
     cp.max_splits = plan.max_splits;
-    cp.seq_len = seq_len;
-    cp.tokens_per_split = plan.pages_per_split * kPage;
     for (int i = 0; i < PGC_CP_MAX_RANKS; ++i) cp.bufs[i] = i < world ? bufs[i] : nullptr;
     cp.world = world;
     cp.rank = rank;
@@ -1102,7 +1088,7 @@ cudaError_t decode_read_error(DevErrorHost *e, bool clear) {
 // library module's load on that device (with CUDA's lazy module loading: the first library
 // call there) until the process exits. Every call shares it and it keeps the last
 // call's contents; nothing in it needs to start at zero, because each call's split kernel
-// writes every partial its merge kernel reads. Two calls that overlap on the GPU (different
+// writes every partial value its merge kernel uses. Two calls that overlap on the GPU (different
 // streams, or different host threads on one device) race on it.
 namespace pgc {
 
