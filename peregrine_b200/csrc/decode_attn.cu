@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int tok_begin = split * p.pages_per_split * kPage;
     if (tok_begin >= L) {
         // A split past the sequence end leaves an empty partial (m = -inf, l = 0; its o is never
-        // read), so the merges take every planned split without reading the lengths again.
+        // summed), so the merges take every planned split without reading the lengths again.
         if (threadIdx.x < nrows) {
             const int j = threadIdx.x / kGroup, g = threadIdx.x % kGroup;
             const int64_t row = (int64_t)(seq * nq + j) * kNumQHeads + kvh * kGroup + g;
@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // (row, 32-dim chunk): lane = dim, so every partial row read is a coalesced 128-byte run, and
 // the 8 warps take every 8th partial, so the reads of different partials are independent and
 // overlap instead of forming one serial chain. A part with m = -inf (a split past the sequence
-// end) has weight 0 and its o is not read.
+// end) has weight 0 and its o is not summed.
 struct MergeParams {
     const float *parts;
     int64_t row_stride;   // floats between rows
